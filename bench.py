@@ -1,0 +1,386 @@
+"""Benchmark: fused PLE forward+backward, feature-embeddings/s and HBM GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5|c4|...] [--impl ours|reference]
+
+One step = the fused forward kernel, the fused backward (kernel + finalize)
+and, with N > 1, one NCCL all-reduce of the packed parameter gradients.
+Under torchrun each rank processes its shard of the configuration's global
+batch (c5: 1,048,576 rows split evenly).  Timing: W warm-up steps, then K
+steps between barrier + synchronize, CUDA events on the compute stream, max
+over ranks.  Inputs (x, upstream gradient) are resident in HBM for ``value``;
+``e2e`` repeats the step through the drop-in module with x copied from
+pinned host memory and the gradients read back every step.  Every step
+moves far more than the 126 MB L2 (c5: ~9 GB per GPU at N=8), so no L2 flush
+is inserted.  ``--impl reference`` times the CPU stand-in for the
+reference's CPU path (upstream dense algorithm, torch CPU, all host
+threads) on a bounded row sample and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "PLE fwd+bwd feature-embeddings/sec & HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
+UNIT = "feature-embeddings/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c5")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        self.t0 = time.time()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in rows for j in range(4) if r[5 + j].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def gpu_id(torch, dev, local):
+    """nvidia-smi id of this rank's GPU (its UUID, robust to CUDA_VISIBLE_DEVICES)."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:  # noqa: BLE001
+        return str(local)
+
+
+def reference_arm(args, ws, rank):
+    """CPU stand-in for the reference's CPU path (rank 0 only)."""
+    if rank != 0:
+        return 0
+    from oracle.cpu_baseline import time_cpu_baseline
+    from piecewiselinearembeddings_optimized_b200 import workloads
+
+    n_global = workloads.SPECS[args.config][0]
+    sample = {"c1": 1024, "c2": 2048, "c3": 512, "c4": 1024, "c5": 1024}[args.config]
+    wl = workloads.make_workload(args.config, n=sample)
+    t0 = time.time()
+    res = time_cpu_baseline(wl, sample, steps=max(1, args.steps), warmup=max(1, args.warmup))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["seconds_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_block(args.config, n_global, args.gpus),
+        "cpu_baseline": {"value": res["value"], "unit": UNIT, "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU path = upstream rtdl_num_embeddings (not installable offline); timed here as "
+                "its dense algorithm restated in torch CPU ops (oracle/cpu_baseline.py)",
+        "wall_s": round(time.time() - t0, 1),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(name, n_global, ws):
+    from piecewiselinearembeddings_optimized_b200 import workloads
+
+    n0, f, d, version, relu, mode, out = workloads.SPECS[name]
+    return {"workload": name, "global_batch": n_global, "n_features": f, "d_embedding": d,
+            "max_n_bins": {"c1": 16, "c2": 48, "c3": 64, "c4": 32, "c5": 64}[name], "version": version,
+            "activation": relu, "x_ple_dtype": mode, "out_dtype": out, "parallelism": f"dp{ws}",
+            "l2": "no flush: every step streams > 126 MB (inputs larger than L2)"}
+
+
+def main() -> int:
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, ws, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import rtdl_num_embeddings_cuda  # noqa: F401  (registers the ops)
+    from piecewiselinearembeddings_optimized_b200 import _native, workloads
+    from piecewiselinearembeddings_optimized_b200.module import CudaPiecewiseLinearEmbeddings, pad_bin_tables
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    name = args.config
+    n0, F, D, version, relu, mode, out_mode = workloads.SPECS[name]
+    n_global = n0
+    n_local = n_global // ws + (1 if rank < n_global % ws else 0)
+    wl_small = workloads.make_workload(name, n=8)  # bins and parameters (independent of the batch)
+    B = wl_small.max_n_bins
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16}
+    q_dtype, o_dtype = dt[mode], dt[out_mode]
+    bins = [torch.from_numpy(b) for b in wl_small.bins]
+    edges, inv_w, n_bins = [t.to(dev) for t in pad_bin_tables(bins)]
+    W = torch.from_numpy(wl_small.weight).to(dev)
+    bias = None if wl_small.bias is None else torch.from_numpy(wl_small.bias).to(dev)
+    w0 = None if wl_small.w0 is None else torch.from_numpy(wl_small.w0).to(dev)
+    b0 = None if wl_small.b0 is None else torch.from_numpy(wl_small.b0).to(dev)
+    epi = 2 if version == "B" else 1
+
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(n_local, F, device=dev, generator=gen)
+    if name == "c4":
+        m = torch.rand(n_local, F, device=dev, generator=gen) < 0.01
+        x[m] = torch.where(torch.rand(n_local, F, device=dev, generator=gen) < 0.5, -10.0, 10.0)[m]
+    g = torch.randn(n_local, F, D, device=dev, generator=gen).to(o_dtype)
+    y = torch.empty(n_local, F, D, device=dev, dtype=o_dtype)
+    gx = torch.empty(n_local, F, device=dev)
+    n_param = F * B * D + (F * D if version == "A" else 2 * F * D)
+    flat = torch.zeros(n_param, device=dev)
+    gW = flat[: F * B * D].view(F, B, D)
+    gb = flat[F * B * D:].view(F, D) if version == "A" else None
+    gw0 = flat[F * B * D: F * B * D + F * D].view(F, D) if version == "B" else None
+    gb0 = flat[F * B * D + F * D:].view(F, D) if version == "B" else None
+    lib = _native.capi()
+    ws_bytes = lib.ple_backward_workspace_size(n_local, F, B, D)
+    wsp = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    code = {torch.float32: 0, torch.bfloat16: 2}
+    P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+
+    def fwd():
+        _native.check(lib.ple_embeddings_forward(
+            x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(), W.data_ptr(), P(bias), P(w0),
+            P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, code[o_dtype], y.data_ptr(), sp), "forward")
+
+    def bwd():
+        _native.check(lib.ple_embeddings_backward(
+            g.data_ptr(), code[o_dtype], x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(),
+            W.data_ptr(), P(bias), P(w0), P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, gx.data_ptr(),
+            gW.data_ptr(), P(gb), P(gw0), P(gb0), wsp.data_ptr(), ws_bytes, sp), "backward")
+
+    def allreduce():
+        if ws > 1:
+            dist.all_reduce(flat)
+
+    # ---------------- warm-up and timed region (device-resident inputs)
+    for _ in range(args.warmup):
+        fwd(); bwd(); allreduce()
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    clocks = ClockSampler(gpu_id(torch, dev, local))
+    clocks.start()
+    time.sleep(0.05)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        ev[k][0].record(stream)
+        fwd()
+        ev[k][1].record(stream)
+        bwd()
+        ev[k][2].record(stream)
+        allreduce()
+        ev[k][3].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    ar_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    t = torch.tensor([total_ms, fwd_ms, bwd_ms, ar_ms], device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, fwd_ms, bwd_ms, ar_ms = [float(v) for v in t.tolist()]
+    ms_per_step = total_ms / args.steps
+    value = n_global * F / (ms_per_step * 1e-3)
+
+    # ---------------- end to end through the drop-in module (host buffers)
+    e2e = None
+    if not args.no_e2e:
+        mod = CudaPiecewiseLinearEmbeddings(bins, D, activation=relu, version=version).to(dev)
+        with torch.no_grad():
+            mod.linear.weight.copy_(W)
+            if bias is not None:
+                mod.linear.bias.copy_(bias)
+            if w0 is not None:
+                mod.linear0.weight.copy_(w0)
+                mod.linear0.bias.copy_(b0)
+        mod.output_dtype = o_dtype
+        x_host = x.cpu().pin_memory()
+        params = list(mod.parameters())
+        out_host = torch.empty(n_param, pin_memory=True)
+        flat2 = torch.zeros(n_param, device=dev)
+
+        def e2e_step():
+            xd = x_host.to(dev, non_blocking=True)
+            for p in params:
+                p.grad = None
+            with torch.autocast("cuda", dtype=q_dtype, enabled=q_dtype != torch.float32):
+                out = mod(xd)
+            out.backward(g)
+            torch.cat([p.grad.reshape(-1) for p in params], out=flat2)
+            if ws > 1:
+                dist.all_reduce(flat2)
+            out_host.copy_(flat2, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if ws > 1:
+            dist.barrier()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        if ws > 1:
+            dist.barrier()
+        te = torch.tensor([a0.elapsed_time(a1)], device=dev)
+        if ws > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item()) / args.steps
+        e2e = {"value": n_global * F / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(x_host.numel() * 4), "d2h_bytes_per_step": int(n_param * 4),
+               "path": "rtdl_num_embeddings_cuda.CudaPiecewiseLinearEmbeddings forward+autograd backward, "
+                       "x from pinned host memory, parameter gradients read back"}
+        del mod, x_host
+
+    if ws > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    # ---------------- roofline of the dominant kernel
+    peak, peak_kind = measured_peak()
+    wl_bytes = workloads.algorithmic_bytes(wl_small, n_local=n_local)
+    kernels = {
+        "forward": {"ms": fwd_ms, "bytes": wl_bytes["fwd"], "gbs": wl_bytes["fwd"] / (fwd_ms * 1e-3) / 1e9},
+        "backward": {"ms": bwd_ms, "bytes": wl_bytes["bwd"], "gbs": wl_bytes["bwd"] / (bwd_ms * 1e-3) / 1e9},
+    }
+    dom = max(kernels, key=lambda k: kernels[k]["ms"])
+    traffic = read_traffic(name, dom)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": kernels[dom]["gbs"] / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6650 GB/s",
+                "traffic": traffic}
+    step_gbs = wl_bytes["step"] / (ms_per_step * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16" if mode == "bf16" else "f32", "data": "synthetic",
+        "config": config_block(name, n_global, ws),
+        "hbm_gbs_per_gpu": step_gbs, "hbm_frac_of_measured": step_gbs / peak, "hbm_frac_of_8tbs": step_gbs / 8000.0,
+        "kernels": {k: {"ms": round(v["ms"], 4), "gb_per_s": round(v["gbs"], 1),
+                        "frac": round(v["gbs"] / peak, 4)} for k, v in kernels.items()},
+        "allreduce_ms": ar_ms, "roofline": roofline, "clocks": clk,
+        "gpu_launches": 3 * args.steps, "e2e": e2e,
+    }
+    if ws == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import time_cpu_baseline
+
+        sample = {"c1": 1024, "c2": 2048, "c3": 1024, "c4": 2048, "c5": 2048}[name]
+        wl_cpu = workloads.make_workload(name, n=sample)
+        cb = time_cpu_baseline(wl_cpu, sample, steps=3, warmup=1)
+        line["cpu_baseline"] = {"value": cb["value"], "unit": UNIT, "cores": cb["cores"], "kind": "port",
+                                "sample": cb["sample"]}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def read_traffic(config: str, kernel: str):
+    """DRAM bytes per launch from a committed ncu summary, if one exists
+    (``profiles/traffic.txt`` lines: ``<config> <kernel> <bytes_per_launch> <note>``)."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == config and parts[1] == kernel:
+            try:
+                return float(parts[2])
+            except ValueError:
+                return None
+    return None
+
+
+if __name__ == "__main__":
+    sys.exit(main())

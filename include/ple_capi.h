@@ -1,0 +1,152 @@
+/*
+ * ple_capi.h - C ABI of the B200-native piecewise-linear embedding (PLE) path.
+ *
+ * Every entry point takes plain device pointers, int64 sizes, dtype codes and
+ * a CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream),
+ * enqueues its kernels on that stream and returns a ple_status (0 = success).
+ * Nothing here allocates device memory: outputs and the backward workspace
+ * are provided by the caller.  Work is asynchronous; launch failures are
+ * reported through the return value, execution faults surface on the stream.
+ *
+ * Shapes (N = batch, F = n_features, B = max_n_bins, D = d_embedding):
+ *   x               [N, F]     float32, row-major contiguous
+ *   bin_edges       [F, B + 1] float32, feature i's n_i + 1 edges then +inf
+ *   inv_bin_widths  [F, B]     float32, 1 / (e[j+1] - e[j]) then 0
+ *   n_bins          [F]        int32, 1 <= n_i <= B
+ *   weight          [F, B, D]  float32, logical bin j < n_i - 1 at row j and
+ *                              the last real bin at row B - 1
+ *   bias            [F, D]     float32 (epilogue A)
+ *   w0, b0          [F, D]     float32 (epilogue B: linear0(x) = x * w0 + b0)
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   ple_forward           csrc/ops.cpp:35-44 -> csrc/forward_cuda.cu:687-860
+ *   ple_backward          csrc/ops.cpp:46-58 -> csrc/backward_cuda.cu:1528-1725
+ *   ple_embeddings_*      src/rtdl_num_embeddings_cuda/module.py:207-248 (forward
+ *                         composition) and its autograd (_autograd.py:42-96 plus
+ *                         the PyTorch epilogue), fused into single kernels.
+ */
+#ifndef PLE_CAPI_H
+#define PLE_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PLE_ABI_VERSION 1
+
+/* Element types (codes shared by every entry point). */
+enum {
+  PLE_DTYPE_F32 = 0,
+  PLE_DTYPE_F16 = 1,
+  PLE_DTYPE_BF16 = 2,
+  PLE_DTYPE_U8 = 3,
+  PLE_DTYPE_I16 = 4,
+  PLE_DTYPE_I32 = 5
+};
+
+/* Epilogue fused after x_ple (module.py:230-248). */
+enum {
+  PLE_EPILOGUE_NONE = 0, /* x_ple only (the reference op)                    */
+  PLE_EPILOGUE_A = 1,    /* act(x_ple + bias)                                */
+  PLE_EPILOGUE_B = 2     /* (x * w0 + b0) + act(x_ple)                       */
+};
+
+/* Status codes. */
+enum {
+  PLE_OK = 0,
+  PLE_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad enum value            */
+  PLE_ERR_SHAPE = 2,            /* non-positive or inconsistent sizes      */
+  PLE_ERR_OVERFLOW = 3,         /* a size overflows the index types        */
+  PLE_ERR_UNSUPPORTED = 4,      /* dtype / size combination not provided   */
+  PLE_ERR_WORKSPACE = 5,        /* workspace missing, small or misaligned  */
+  PLE_ERR_CUDA = 6,             /* a CUDA runtime call failed              */
+  PLE_ERR_ALIGNMENT = 7         /* a pointer is not 16-byte aligned        */
+};
+
+/* ABI version of the loaded library (PLE_ABI_VERSION at build time). */
+int ple_abi_version(void);
+
+/* Static description of a status code. */
+const char* ple_status_string(int status);
+
+/* Detail message of the last failing call on the calling host thread. */
+const char* ple_last_error_message(void);
+
+/*
+ * x_ple forward (reference op rtdl_num_embeddings_cuda::forward).
+ *   output[N, F, D] in output_dtype (F32 / F16 / BF16):
+ *     x_ple[b,i,:] = sum_{j<k} q(W[i,j,:]) + q(t) * q(W[i,phys(k),:])
+ *   with k the right-sided clamped bin of x[b,i], t = (x - e_k) * r_k and q()
+ *   rounding through output_dtype (autocast emulation, fp32 accumulation).
+ *   bin_indices[N, F] (optional, may be NULL) receives k as U8 / I16 / I32
+ *   according to bin_index_dtype.
+ */
+int ple_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                const int32_t* n_bins, const float* weight, int64_t batch,
+                int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                int output_dtype, void* output, int bin_index_dtype, void* bin_indices,
+                void* stream);
+
+/*
+ * Workspace bytes ple_backward / ple_embeddings_backward need for these sizes
+ * (per-partition partial sums of the parameter gradients; 0 never returned).
+ */
+size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t max_n_bins,
+                                   int64_t d_embedding);
+
+/*
+ * x_ple backward (reference op rtdl_num_embeddings_cuda::backward).
+ *   grad_output[N, F, D] in grad_dtype (F32 / F16 / BF16).
+ *   grad_x[N, F] (may be NULL):
+ *     r_k <g, q(W[phys k])> + [k > 0 and x == e_k] r_{k-1} <g, q(W[k-1])>
+ *   grad_weight[F, B, D] (may be NULL; padding rows are written as zero):
+ *     grad_W[i, phys(j)] = sum_{k_b = j} q(t_b) g_b + sum_{k_b > j} g_b
+ *   bin_indices is accepted for interface parity and may be NULL; bins are
+ *   recomputed from x.  The result is bitwise deterministic.
+ */
+int ple_backward(const void* grad_output, int grad_dtype, const float* x,
+                 const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
+                 const float* weight, const void* bin_indices, int bin_index_dtype,
+                 int64_t batch, int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                 float* grad_x, float* grad_weight, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/*
+ * Fused embeddings forward (the whole module forward in one kernel):
+ *   epilogue A: y = act(x_ple + bias); epilogue B: y = (x * w0 + b0) + act(x_ple)
+ *   act = ReLU when activation != 0.  x_ple is computed as in ple_forward with
+ *   rounding through compute_dtype (F32 = plain fp32; BF16 / F16 = autocast);
+ *   the epilogue runs in fp32 and the result is stored as output_dtype.
+ */
+int ple_embeddings_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                           const int32_t* n_bins, const float* weight, const float* bias,
+                           const float* w0, const float* b0, int epilogue, int activation,
+                           int compute_dtype, int64_t batch, int64_t n_features,
+                           int64_t max_n_bins, int64_t d_embedding, int output_dtype,
+                           void* output, void* stream);
+
+/*
+ * Fused embeddings backward: every gradient of ple_embeddings_forward from the
+ * upstream gradient in one pass over grad_output.  Gradient pointers may be
+ * NULL when not needed; grad_bias is used with epilogue A, grad_w0 / grad_b0
+ * with epilogue B.  Parameter gradients are written (not accumulated) and are
+ * bitwise deterministic.
+ */
+int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float* x,
+                            const float* bin_edges, const float* inv_bin_widths,
+                            const int32_t* n_bins, const float* weight, const float* bias,
+                            const float* w0, const float* b0, int epilogue, int activation,
+                            int compute_dtype, int64_t batch, int64_t n_features,
+                            int64_t max_n_bins, int64_t d_embedding, float* grad_x,
+                            float* grad_weight, float* grad_bias, float* grad_w0,
+                            float* grad_b0, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLE_CAPI_H */

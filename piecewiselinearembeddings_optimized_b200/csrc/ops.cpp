@@ -1,0 +1,259 @@
+// ops.cpp - torch op registration for rtdl_num_embeddings_cuda (the only
+// torch-facing layer).  Validates like the reference (TORCH_CHECK with the
+// same conditions), allocates outputs and the backward workspace from the
+// ATen caching allocator on the input's device, and calls the C ABI of
+// libple_b200.so on the current CUDA stream.
+//
+// Schemas kept verbatim from the reference (ops.cpp:35-58):
+//   forward(x, bin_edges, inv_bin_widths, n_bins, weight, output_dtype) -> (output, bin_indices)
+//   backward(grad_output, x, bin_edges, inv_bin_widths, n_bins, weight, bin_indices,
+//            compute_grad_x, compute_grad_weight) -> (grad_x, grad_weight)
+// Added (the fused module path):
+//   embeddings_forward / embeddings_backward.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <optional>
+#include <tuple>
+
+#include "ple_capi.h"
+
+namespace {
+
+int to_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return PLE_DTYPE_F32;
+    case at::kHalf: return PLE_DTYPE_F16;
+    case at::kBFloat16: return PLE_DTYPE_BF16;
+    case at::kByte: return PLE_DTYPE_U8;
+    case at::kShort: return PLE_DTYPE_I16;
+    case at::kInt: return PLE_DTYPE_I32;
+    default: return -1;
+  }
+}
+
+at::ScalarType bin_index_dtype(int64_t max_n_bins) {
+  return max_n_bins <= 256 ? at::kByte : (max_n_bins <= 32768 ? at::kShort : at::kInt);
+}
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == PLE_OK, what, " failed: ", ple_status_string(st), ": ", ple_last_error_message());
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(c10::cuda::getCurrentCUDAStream(t.get_device()).stream());
+}
+
+void check_tables(const at::Tensor& x, const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
+                  const at::Tensor& n_bins, const at::Tensor& weight) {
+  TORCH_CHECK(x.is_cuda(), "x must be a CUDA tensor");
+  TORCH_CHECK(bin_edges.is_cuda(), "bin_edges must be a CUDA tensor");
+  TORCH_CHECK(inv_bin_widths.is_cuda(), "inv_bin_widths must be a CUDA tensor");
+  TORCH_CHECK(n_bins.is_cuda(), "n_bins must be a CUDA tensor");
+  TORCH_CHECK(weight.is_cuda(), "weight must be a CUDA tensor");
+  TORCH_CHECK(x.device() == bin_edges.device() && x.device() == inv_bin_widths.device() &&
+                  x.device() == n_bins.device() && x.device() == weight.device(),
+              "All forward tensors must be on the same CUDA device");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  TORCH_CHECK(bin_edges.is_contiguous(), "bin_edges must be contiguous");
+  TORCH_CHECK(inv_bin_widths.is_contiguous(), "inv_bin_widths must be contiguous");
+  TORCH_CHECK(n_bins.is_contiguous(), "n_bins must be contiguous");
+  TORCH_CHECK(weight.is_contiguous(), "weight must be contiguous");
+  TORCH_CHECK(x.dim() == 2, "x must have shape [N, F]");
+  TORCH_CHECK(bin_edges.dim() == 2, "bin_edges must have shape [F, B + 1]");
+  TORCH_CHECK(inv_bin_widths.dim() == 2, "inv_bin_widths must have shape [F, B]");
+  TORCH_CHECK(n_bins.dim() == 1, "n_bins must have shape [F]");
+  TORCH_CHECK(weight.dim() == 3, "weight must have shape [F, B, D]");
+  TORCH_CHECK(x.scalar_type() == at::kFloat, "x must be float32");
+  TORCH_CHECK(bin_edges.scalar_type() == at::kFloat, "bin_edges must be float32");
+  TORCH_CHECK(inv_bin_widths.scalar_type() == at::kFloat, "inv_bin_widths must be float32");
+  TORCH_CHECK(n_bins.scalar_type() == at::kInt, "n_bins must be int32");
+  TORCH_CHECK(weight.scalar_type() == at::kFloat, "weight parameters must be float32");
+  const int64_t F = x.size(1), B = weight.size(1);
+  TORCH_CHECK(F > 0, "n_features must be positive");
+  TORCH_CHECK(B > 0, "max_n_bins must be positive");
+  TORCH_CHECK(weight.size(2) > 0, "d_embedding must be positive");
+  TORCH_CHECK(weight.size(0) == F, "weight.size(0) must equal x.size(1)");
+  TORCH_CHECK(bin_edges.size(0) == F, "bin_edges.size(0) must equal x.size(1)");
+  TORCH_CHECK(bin_edges.size(1) == B + 1, "bin_edges.size(1) must equal max_n_bins + 1");
+  TORCH_CHECK(inv_bin_widths.size(0) == F, "inv_bin_widths.size(0) must equal x.size(1)");
+  TORCH_CHECK(inv_bin_widths.size(1) == B, "inv_bin_widths.size(1) must equal max_n_bins");
+  TORCH_CHECK(n_bins.size(0) == F, "n_bins.size(0) must equal x.size(1)");
+}
+
+void check_param(const std::optional<at::Tensor>& p, const at::Tensor& weight, const char* name) {
+  if (!p.has_value()) return;
+  TORCH_CHECK(p->is_cuda() && p->device() == weight.device(), name, " must be on the weight's CUDA device");
+  TORCH_CHECK(p->scalar_type() == at::kFloat, name, " must be float32");
+  TORCH_CHECK(p->is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(p->dim() == 2 && p->size(0) == weight.size(0) && p->size(1) == weight.size(2), name,
+              " must have shape [F, D]");
+}
+
+const float* ptr_or_null(const std::optional<at::Tensor>& p) {
+  return p.has_value() ? p->data_ptr<float>() : nullptr;
+}
+
+std::tuple<at::Tensor, at::Tensor> ple_forward_op(const at::Tensor& x, const at::Tensor& bin_edges,
+                                                  const at::Tensor& inv_bin_widths, const at::Tensor& n_bins,
+                                                  const at::Tensor& weight, at::ScalarType output_dtype) {
+  check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
+  TORCH_CHECK(output_dtype == at::kFloat || output_dtype == at::kHalf || output_dtype == at::kBFloat16,
+              "output_dtype must be float32, float16, or bfloat16");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  at::Tensor out = at::empty({N, F, D}, weight.options().dtype(output_dtype));
+  const at::ScalarType idx_t = bin_index_dtype(B);
+  at::Tensor idx = at::empty({N, F}, weight.options().dtype(idx_t));
+  if (out.numel() == 0) return {out, idx};
+  check_status(ple_forward(x.data_ptr<float>(), bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                           n_bins.data_ptr<int32_t>(), weight.data_ptr<float>(), N, F, B, D,
+                           to_code(output_dtype), out.data_ptr(), to_code(idx_t), idx.data_ptr(),
+                           stream_of(x)),
+               "rtdl_num_embeddings_cuda::forward");
+  return {out, idx};
+}
+
+at::Tensor workspace_for(const at::Tensor& like, int64_t N, int64_t F, int64_t B, int64_t D) {
+  const size_t bytes = ple_backward_workspace_size(N, F, B, D);
+  return at::empty({(int64_t)bytes}, like.options().dtype(at::kByte));
+}
+
+std::tuple<at::Tensor, at::Tensor> ple_backward_op(const at::Tensor& grad_output, const at::Tensor& x,
+                                                   const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
+                                                   const at::Tensor& n_bins, const at::Tensor& weight,
+                                                   const at::Tensor& bin_indices, bool compute_grad_x,
+                                                   bool compute_grad_weight) {
+  TORCH_CHECK(grad_output.is_cuda(), "grad_output must be CUDA");
+  TORCH_CHECK(bin_indices.is_cuda(), "bin_indices must be CUDA");
+  check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
+  TORCH_CHECK(grad_output.device() == x.device() && bin_indices.device() == x.device(),
+              "All backward tensors must be on the same CUDA device");
+  TORCH_CHECK(grad_output.is_contiguous(), "grad_output must be contiguous");
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  TORCH_CHECK(grad_output.scalar_type() == at::kFloat || grad_output.scalar_type() == at::kHalf ||
+                  grad_output.scalar_type() == at::kBFloat16,
+              "grad_output must be float32, float16, or bfloat16");
+  TORCH_CHECK(bin_indices.scalar_type() == bin_index_dtype(B), "bin_indices has an invalid dtype");
+  TORCH_CHECK(grad_output.dim() == 3 && grad_output.size(0) == N && grad_output.size(1) == F &&
+                  grad_output.size(2) == D,
+              "grad_output shape must be [N, F, D]");
+  TORCH_CHECK(bin_indices.dim() == 2 && bin_indices.size(0) == N && bin_indices.size(1) == F,
+              "bin_indices shape must be [N, F]");
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor grad_x = compute_grad_x ? at::empty_like(x) : at::empty({0}, x.options());
+  at::Tensor grad_w = compute_grad_weight ? at::empty_like(weight) : at::empty({0}, weight.options());
+  if (!compute_grad_x && !compute_grad_weight) return {grad_x, grad_w};
+  at::Tensor ws = workspace_for(x, N, F, B, D);
+  check_status(ple_backward(grad_output.data_ptr(), to_code(grad_output.scalar_type()), x.data_ptr<float>(),
+                            bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                            n_bins.data_ptr<int32_t>(), weight.data_ptr<float>(), bin_indices.data_ptr(),
+                            to_code(bin_indices.scalar_type()), N, F, B, D,
+                            compute_grad_x ? grad_x.data_ptr<float>() : nullptr,
+                            compute_grad_weight ? grad_w.data_ptr<float>() : nullptr, ws.data_ptr(),
+                            (size_t)ws.numel(), stream_of(x)),
+               "rtdl_num_embeddings_cuda::backward");
+  return {grad_x, grad_w};
+}
+
+at::Tensor ple_embeddings_forward_op(const at::Tensor& x, const at::Tensor& bin_edges,
+                                     const at::Tensor& inv_bin_widths, const at::Tensor& n_bins,
+                                     const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+                                     const std::optional<at::Tensor>& w0, const std::optional<at::Tensor>& b0,
+                                     int64_t epilogue, bool activation, at::ScalarType compute_dtype,
+                                     at::ScalarType output_dtype) {
+  check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
+  check_param(bias, weight, "bias");
+  check_param(w0, weight, "w0");
+  check_param(b0, weight, "b0");
+  TORCH_CHECK(to_code(output_dtype) >= 0 && to_code(output_dtype) <= PLE_DTYPE_BF16,
+              "output_dtype must be float32, float16, or bfloat16");
+  TORCH_CHECK(to_code(compute_dtype) >= 0 && to_code(compute_dtype) <= PLE_DTYPE_BF16,
+              "compute_dtype must be float32, float16, or bfloat16");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  at::Tensor out = at::empty({N, F, D}, weight.options().dtype(output_dtype));
+  if (out.numel() == 0) return out;
+  check_status(ple_embeddings_forward(x.data_ptr<float>(), bin_edges.data_ptr<float>(),
+                                      inv_bin_widths.data_ptr<float>(), n_bins.data_ptr<int32_t>(),
+                                      weight.data_ptr<float>(), ptr_or_null(bias), ptr_or_null(w0),
+                                      ptr_or_null(b0), (int)epilogue, activation ? 1 : 0,
+                                      to_code(compute_dtype), N, F, B, D, to_code(output_dtype), out.data_ptr(),
+                                      stream_of(x)),
+               "rtdl_num_embeddings_cuda::embeddings_forward");
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embeddings_backward_op(
+    const at::Tensor& grad_output, const at::Tensor& x, const at::Tensor& bin_edges,
+    const at::Tensor& inv_bin_widths, const at::Tensor& n_bins, const at::Tensor& weight,
+    const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& w0,
+    const std::optional<at::Tensor>& b0, int64_t epilogue, bool activation, at::ScalarType compute_dtype,
+    bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, bool compute_grad_linear0) {
+  check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
+  check_param(bias, weight, "bias");
+  check_param(w0, weight, "w0");
+  check_param(b0, weight, "b0");
+  TORCH_CHECK(grad_output.is_cuda() && grad_output.device() == x.device(),
+              "grad_output must be on x's CUDA device");
+  TORCH_CHECK(grad_output.is_contiguous(), "grad_output must be contiguous");
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  TORCH_CHECK(grad_output.dim() == 3 && grad_output.size(0) == N && grad_output.size(1) == F &&
+                  grad_output.size(2) == D,
+              "grad_output shape must be [N, F, D]");
+  TORCH_CHECK(to_code(grad_output.scalar_type()) >= 0 && to_code(grad_output.scalar_type()) <= PLE_DTYPE_BF16,
+              "grad_output must be float32, float16, or bfloat16");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto opt = weight.options();
+  const bool want_bias = compute_grad_bias && epilogue == PLE_EPILOGUE_A;
+  const bool want_l0 = compute_grad_linear0 && epilogue == PLE_EPILOGUE_B;
+  at::Tensor gx = compute_grad_x ? at::empty_like(x) : at::empty({0}, x.options());
+  at::Tensor gw = compute_grad_weight ? at::empty_like(weight) : at::empty({0}, opt);
+  at::Tensor gb = want_bias ? at::empty({F, D}, opt) : at::empty({0}, opt);
+  at::Tensor gw0 = want_l0 ? at::empty({F, D}, opt) : at::empty({0}, opt);
+  at::Tensor gb0 = want_l0 ? at::empty({F, D}, opt) : at::empty({0}, opt);
+  if (!compute_grad_x && !compute_grad_weight && !want_bias && !want_l0) return {gx, gw, gb, gw0, gb0};
+  at::Tensor ws = workspace_for(x, N, F, B, D);
+  check_status(ple_embeddings_backward(
+                   grad_output.data_ptr(), to_code(grad_output.scalar_type()), x.data_ptr<float>(),
+                   bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(), n_bins.data_ptr<int32_t>(),
+                   weight.data_ptr<float>(), ptr_or_null(bias), ptr_or_null(w0), ptr_or_null(b0), (int)epilogue,
+                   activation ? 1 : 0, to_code(compute_dtype), N, F, B, D,
+                   compute_grad_x ? gx.data_ptr<float>() : nullptr,
+                   compute_grad_weight ? gw.data_ptr<float>() : nullptr, want_bias ? gb.data_ptr<float>() : nullptr,
+                   want_l0 ? gw0.data_ptr<float>() : nullptr, want_l0 ? gb0.data_ptr<float>() : nullptr,
+                   ws.data_ptr(), (size_t)ws.numel(), stream_of(x)),
+               "rtdl_num_embeddings_cuda::embeddings_backward");
+  return {gx, gw, gb, gw0, gb0};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
+  m.def(
+      "forward(Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, Tensor weight, "
+      "ScalarType output_dtype) -> (Tensor output, Tensor bin_indices)");
+  m.def(
+      "backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, "
+      "Tensor weight, Tensor bin_indices, bool compute_grad_x, bool compute_grad_weight) -> "
+      "(Tensor grad_x, Tensor grad_weight)");
+  m.def(
+      "embeddings_forward(Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, Tensor weight, "
+      "Tensor? bias, Tensor? w0, Tensor? b0, int epilogue, bool activation, ScalarType compute_dtype, "
+      "ScalarType output_dtype) -> Tensor");
+  m.def(
+      "embeddings_backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, "
+      "Tensor n_bins, Tensor weight, Tensor? bias, Tensor? w0, Tensor? b0, int epilogue, bool activation, "
+      "ScalarType compute_dtype, bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, "
+      "bool compute_grad_linear0) -> (Tensor grad_x, Tensor grad_weight, Tensor grad_bias, Tensor grad_w0, "
+      "Tensor grad_b0)");
+}
+
+TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
+  m.impl("forward", &ple_forward_op);
+  m.impl("backward", &ple_backward_op);
+  m.impl("embeddings_forward", &ple_embeddings_forward_op);
+  m.impl("embeddings_backward", &ple_embeddings_backward_op);
+}

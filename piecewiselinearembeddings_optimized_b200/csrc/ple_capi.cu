@@ -1,0 +1,256 @@
+// ple_capi.cu - extern "C" entry points of libple_b200.so.
+//
+// Validation mirrors the reference's TORCH_CHECKs (forward_cuda.cu:695-790,
+// backward_cuda.cu:1539-1657) as status codes; the torch adapter (ops.cpp)
+// turns a non-zero status into a RuntimeError with ple_last_error_message().
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "ple_common.cuh"
+#include "ple_internal.h"
+
+namespace ple {
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* msg) {
+  snprintf(g_msg, sizeof(g_msg), "%s", msg);
+  return code;
+}
+
+int set_cuda_error(cudaError_t e, const char* what) {
+  snprintf(g_msg, sizeof(g_msg), "%s: %s", what, cudaGetErrorString(e));
+  return PLE_ERR_CUDA;
+}
+
+namespace {
+struct DevProps {
+  int sms = 0;
+  size_t smem_optin = 0;
+};
+constexpr int kMaxDevices = 64;
+DevProps g_props[kMaxDevices];
+std::once_flag g_once[kMaxDevices];
+
+const DevProps& props() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  std::call_once(g_once[dev], [dev] {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    g_props[dev].sms = v > 0 ? v : 1;
+    v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    g_props[dev].smem_optin = v > 0 ? (size_t)v : 48 * 1024;
+  });
+  return g_props[dev];
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int dtype_size(int dt) {
+  switch (dt) {
+    case PLE_DTYPE_F32: return 4;
+    case PLE_DTYPE_F16: case PLE_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+int check_sizes(int64_t N, int64_t F, int64_t B, int64_t D) {
+  if (N < 0) return set_error(PLE_ERR_SHAPE, "batch must be >= 0");
+  if (F <= 0) return set_error(PLE_ERR_SHAPE, "n_features must be positive");
+  if (B <= 0) return set_error(PLE_ERR_SHAPE, "max_n_bins must be positive");
+  if (D <= 0) return set_error(PLE_ERR_SHAPE, "d_embedding must be positive");
+  if (D > kMaxD) return set_error(PLE_ERR_UNSUPPORTED, "d_embedding must be <= 64");
+  if (B > 256) return set_error(PLE_ERR_UNSUPPORTED, "max_n_bins > 256 is not supported by the sm_100a kernels");
+  if (F > (int64_t)1 << 30) return set_error(PLE_ERR_OVERFLOW, "n_features too large");
+  if (N > 0 && F > INT64_MAX / N / D) return set_error(PLE_ERR_OVERFLOW, "N * F * D overflows int64");
+  return PLE_OK;
+}
+
+int check_tables(const float* edges, const float* inv_w, const int32_t* n_bins, const float* W) {
+  if (!edges || !inv_w || !n_bins || !W)
+    return set_error(PLE_ERR_INVALID_ARGUMENT, "bin_edges, inv_bin_widths, n_bins and weight are required");
+  return PLE_OK;
+}
+
+// Widest vector width (elements) such that D is a multiple and every listed
+// pointer is aligned for it.
+int pick_vec(int64_t D, int max_vec, std::initializer_list<std::pair<const void*, int>> ptrs) {
+  for (int v = max_vec; v > 1; v >>= 1) {
+    if (D % v) continue;
+    bool ok = true;
+    for (auto& pe : ptrs)
+      if (pe.first && !aligned(pe.first, (size_t)v * pe.second)) ok = false;
+    if (ok) return v;
+  }
+  return 1;
+}
+}  // namespace
+
+int device_sm_count() { return props().sms; }
+size_t device_max_smem_optin() { return props().smem_optin; }
+
+int backward_vec(int64_t D) {
+  if (D % 8 == 0 && D >= 48) return 8;
+  if (D % 4 == 0) return 4;
+  if (D % 2 == 0) return 2;
+  return 1;
+}
+
+}  // namespace ple
+
+using namespace ple;
+
+extern "C" {
+
+int ple_abi_version(void) { return PLE_ABI_VERSION; }
+
+const char* ple_status_string(int status) {
+  switch (status) {
+    case PLE_OK: return "ok";
+    case PLE_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PLE_ERR_SHAPE: return "invalid shape";
+    case PLE_ERR_OVERFLOW: return "size overflow";
+    case PLE_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PLE_ERR_WORKSPACE: return "workspace missing or too small";
+    case PLE_ERR_CUDA: return "CUDA error";
+    case PLE_ERR_ALIGNMENT: return "misaligned pointer";
+    default: return "unknown status";
+  }
+}
+
+const char* ple_last_error_message(void) { return g_msg; }
+
+static int forward_impl(const float* x, const float* edges, const float* inv_w, const int32_t* n_bins,
+                        const float* W, const float* bias, const float* w0, const float* b0, int epi,
+                        int relu, int compute_dtype, int64_t N, int64_t F, int64_t B, int64_t D,
+                        int out_dtype, void* out, int bin_idx_dtype, void* bin_idx, void* stream) {
+  g_msg[0] = 0;
+  int st = check_sizes(N, F, B, D);
+  if (st) return st;
+  if ((st = check_tables(edges, inv_w, n_bins, W))) return st;
+  if (dtype_size(out_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "output dtype must be F32, F16 or BF16");
+  if (dtype_size(compute_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "compute dtype must be F32, F16 or BF16");
+  if (epi != kEpiNone && epi != kEpiA && epi != kEpiB) return set_error(PLE_ERR_INVALID_ARGUMENT, "bad epilogue");
+  if (epi == kEpiA && !bias) return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue A needs bias");
+  if (epi == kEpiB && (!w0 || !b0)) return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue B needs w0 and b0");
+  int idx_bytes = 0;
+  if (bin_idx) {
+    switch (bin_idx_dtype) {
+      case PLE_DTYPE_U8: idx_bytes = 1; break;
+      case PLE_DTYPE_I16: idx_bytes = 2; break;
+      case PLE_DTYPE_I32: idx_bytes = 4; break;
+      default: return set_error(PLE_ERR_INVALID_ARGUMENT, "bin index dtype must be U8, I16 or I32");
+    }
+    if (idx_bytes == 1 && B > 256) return set_error(PLE_ERR_INVALID_ARGUMENT, "U8 bin indices need max_n_bins <= 256");
+  }
+  if (N == 0) return PLE_OK;
+  if (!x || !out) return set_error(PLE_ERR_INVALID_ARGUMENT, "x and output are required");
+  FwdArgs a{};
+  a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.W = W;
+  a.bias = bias; a.w0 = w0; a.b0 = b0; a.out = out; a.bin_idx = bin_idx; a.bin_idx_bytes = idx_bytes;
+  a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D; a.epi = epi; a.relu = relu ? 1 : 0;
+  const int vec = pick_vec(D, 4, {{out, dtype_size(out_dtype)}, {bias, 4}, {w0, 4}, {b0, 4}});
+  return launch_forward(a, compute_dtype, out_dtype, vec, static_cast<cudaStream_t>(stream));
+}
+
+int ple_forward(const float* x, const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
+                const float* weight, int64_t batch, int64_t n_features, int64_t max_n_bins,
+                int64_t d_embedding, int output_dtype, void* output, int bin_index_dtype,
+                void* bin_indices, void* stream) {
+  return forward_impl(x, bin_edges, inv_bin_widths, n_bins, weight, nullptr, nullptr, nullptr, kEpiNone, 0,
+                      output_dtype, batch, n_features, max_n_bins, d_embedding, output_dtype, output,
+                      bin_index_dtype, bin_indices, stream);
+}
+
+int ple_embeddings_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                           const int32_t* n_bins, const float* weight, const float* bias, const float* w0,
+                           const float* b0, int epilogue, int activation, int compute_dtype, int64_t batch,
+                           int64_t n_features, int64_t max_n_bins, int64_t d_embedding, int output_dtype,
+                           void* output, void* stream) {
+  return forward_impl(x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, epilogue, activation,
+                      compute_dtype, batch, n_features, max_n_bins, d_embedding, output_dtype, output,
+                      PLE_DTYPE_U8, nullptr, stream);
+}
+
+size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t max_n_bins,
+                                   int64_t d_embedding) {
+  if (check_sizes(batch, n_features, max_n_bins, d_embedding) != PLE_OK) return 0;
+  size_t b = backward_workspace_bytes(batch < 1 ? 1 : batch, n_features, max_n_bins, d_embedding);
+  return b ? b : 16;
+}
+
+static int backward_impl(const void* g, int grad_dtype, const float* x, const float* edges, const float* inv_w,
+                         const int32_t* n_bins, const float* W, const float* bias, const float* w0,
+                         const float* b0, int epi, int relu, int compute_dtype, int64_t N, int64_t F,
+                         int64_t B, int64_t D, float* grad_x, float* grad_W, float* grad_bias,
+                         float* grad_w0, float* grad_b0, void* ws, size_t ws_bytes, void* stream) {
+  g_msg[0] = 0;
+  int st = check_sizes(N, F, B, D);
+  if (st) return st;
+  if ((st = check_tables(edges, inv_w, n_bins, W))) return st;
+  if (dtype_size(grad_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad dtype must be F32, F16 or BF16");
+  if (dtype_size(compute_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "compute dtype must be F32, F16 or BF16");
+  if (epi != kEpiNone && epi != kEpiA && epi != kEpiB) return set_error(PLE_ERR_INVALID_ARGUMENT, "bad epilogue");
+  if (epi == kEpiA && relu && !bias) return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue A with ReLU needs bias");
+  if (epi == kEpiB && (grad_x || grad_w0 || grad_b0) && !w0)
+    return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue B needs w0");
+  if (epi != kEpiA) grad_bias = nullptr;
+  if (epi != kEpiB) { grad_w0 = nullptr; grad_b0 = nullptr; }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool any_param = grad_W || grad_bias || grad_w0 || grad_b0;
+  if (!grad_x && !any_param) return PLE_OK;
+  if (N == 0) {
+    // no samples: parameter gradients are zero (reference zeros_like, backward_cuda.cu:1661-1670)
+    cudaError_t e = cudaSuccess;
+    if (grad_W) e = cudaMemsetAsync(grad_W, 0, (size_t)F * B * D * 4, s);
+    if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, (size_t)F * D * 4, s);
+    if (e == cudaSuccess && grad_w0) e = cudaMemsetAsync(grad_w0, 0, (size_t)F * D * 4, s);
+    if (e == cudaSuccess && grad_b0) e = cudaMemsetAsync(grad_b0, 0, (size_t)F * D * 4, s);
+    return e == cudaSuccess ? PLE_OK : set_cuda_error(e, "cudaMemsetAsync");
+  }
+  if (!g || !x) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad_output and x are required");
+  if (!ws) return set_error(PLE_ERR_WORKSPACE, "backward needs a workspace (ple_backward_workspace_size)");
+  if (!aligned(ws, 16)) return set_error(PLE_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+  const int vec = backward_vec(D);
+  if (D / vec > 32) return set_error(PLE_ERR_UNSUPPORTED, "backward: odd d_embedding above 32 is not supported");
+  if (!aligned(g, (size_t)vec * dtype_size(grad_dtype)) || !aligned(w0, (size_t)vec * 4) ||
+      !aligned(bias, (size_t)vec * 4))
+    return set_error(PLE_ERR_ALIGNMENT, "grad_output / bias / w0 must be aligned to the vector width");
+  BwdArgs a{};
+  a.g = g; a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.W = W;
+  a.bias = bias; a.w0 = w0; a.b0 = b0;
+  a.grad_x = grad_x; a.grad_W = grad_W; a.grad_bias = grad_bias; a.grad_w0 = grad_w0; a.grad_b0 = grad_b0;
+  a.ws = static_cast<float*>(ws); a.ws_bytes = ws_bytes;
+  a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D; a.epi = epi; a.relu = relu ? 1 : 0;
+  return launch_backward(a, compute_dtype, grad_dtype, vec, s);
+}
+
+int ple_backward(const void* grad_output, int grad_dtype, const float* x, const float* bin_edges,
+                 const float* inv_bin_widths, const int32_t* n_bins, const float* weight,
+                 const void* bin_indices, int bin_index_dtype, int64_t batch, int64_t n_features,
+                 int64_t max_n_bins, int64_t d_embedding, float* grad_x, float* grad_weight, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  (void)bin_indices;
+  (void)bin_index_dtype;
+  return backward_impl(grad_output, grad_dtype, x, bin_edges, inv_bin_widths, n_bins, weight, nullptr, nullptr,
+                       nullptr, kEpiNone, 0, grad_dtype, batch, n_features, max_n_bins, d_embedding, grad_x,
+                       grad_weight, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float* x, const float* bin_edges,
+                            const float* inv_bin_widths, const int32_t* n_bins, const float* weight,
+                            const float* bias, const float* w0, const float* b0, int epilogue, int activation,
+                            int compute_dtype, int64_t batch, int64_t n_features, int64_t max_n_bins,
+                            int64_t d_embedding, float* grad_x, float* grad_weight, float* grad_bias,
+                            float* grad_w0, float* grad_b0, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  return backward_impl(grad_output, grad_dtype, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0,
+                       epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, grad_x,
+                       grad_weight, grad_bias, grad_w0, grad_b0, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,80 @@
+// ple_internal.h - launch arguments and host helpers shared by the .cu files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/ple_capi.h"
+
+namespace ple {
+
+enum { kEpiNone = PLE_EPILOGUE_NONE, kEpiA = PLE_EPILOGUE_A, kEpiB = PLE_EPILOGUE_B };
+
+// backward tuning
+constexpr int kBwdThreads = 512;
+constexpr int kBwdTile = 1024;
+constexpr size_t kBwdSmemTwoCtas = 112 * 1024;
+
+// forward tuning
+constexpr int kFwdMaxThreads = 256;
+constexpr size_t kFwdTableBudget = 64 * 1024;
+constexpr int kFwdPairsPerTile = 2048;
+
+struct FwdArgs {
+  const float* x;
+  const float* edges;
+  const float* inv_w;
+  const int32_t* n_bins;
+  const float* W;
+  const float* bias;
+  const float* w0;
+  const float* b0;
+  void* out;
+  void* bin_idx;
+  int bin_idx_bytes;
+  int64_t N;
+  int F, B, D;
+  int epi, relu;
+  // filled by the launcher
+  int Fc, n_chunks, n_parts, S_t, pow2;
+};
+
+struct BwdArgs {
+  const void* g;
+  const float* x;
+  const float* edges;
+  const float* inv_w;
+  const int32_t* n_bins;
+  const float* W;
+  const float* bias;
+  const float* w0;
+  const float* b0;
+  float* grad_x;
+  float* grad_W;
+  float* grad_bias;
+  float* grad_w0;
+  float* grad_b0;
+  float* ws;          // partials: [n_parts][F][B + 3][D] floats
+  size_t ws_bytes;
+  int64_t N;
+  int F, B, D;
+  int epi, relu;
+  // filled by the launcher
+  int Fc, Wf, n_chunks, n_parts, S_t, pow2;
+};
+
+// error plumbing (ple_capi.cu)
+int set_error(int code, const char* msg);
+int set_cuda_error(cudaError_t e, const char* what);
+
+// cached properties of the current device (ple_capi.cu)
+int device_sm_count();
+size_t device_max_smem_optin();
+
+int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cudaStream_t st);
+int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
+int backward_vec(int64_t D);
+size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
+
+}  // namespace ple
