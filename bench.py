@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c5")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=None, help="override the global batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -180,7 +181,7 @@ def main() -> int:
 
     name = args.config
     n0, F, D, version, relu, mode, out_mode = workloads.SPECS[name]
-    n_global = n0
+    n_global = args.batch or n0
     n_local = n_global // ws + (1 if rank < n_global % ws else 0)
     wl_small = workloads.make_workload(name, n=8)  # bins and parameters (independent of the batch)
     B = wl_small.max_n_bins

@@ -19,7 +19,7 @@ Two independent formulations live here:
   Features in Tabular Deep Learning", piecewise-linear encoding, eq. 1) and is
   used as an independent cross-check and as the CPU baseline.
 
-Pinning: ``tests/test_oracle_golden.py`` checks the pairwise restatement
+Pinning: ``tests/test_oracle.py`` checks the pairwise restatement
 against golden vectors produced by the reference's own CUDA ops
 (``tests/golden/make_golden.py``, compiled from the reference sources by
 ``oracle/build_ref.py``).
@@ -189,7 +189,7 @@ def x_ple_forward(x, edges, inv_w, n_bins, W, mode: str = "f32"):
     return quantize(out, mode), k
 
 
-def x_ple_backward(g, x, edges, inv_w, n_bins, W, mode: str = "f32"):
+def x_ple_backward(g, x, edges, inv_w, n_bins, W, mode: str = "f32", with_abs: bool = False):
     """Gradients of ``x_ple`` with respect to ``x`` and ``weight``.
 
     * ``grad_x = r_k <g, q(W[phys k])> + [k>0 and x == e_k] r_{k-1} <g, q(W[k-1])>``
@@ -199,7 +199,9 @@ def x_ple_backward(g, x, edges, inv_w, n_bins, W, mode: str = "f32"):
       ``j < n_i`` and zero in padding rows (reverse prefix over bins,
       backward_cuda.cu:268-336 and 859-925).
 
-    Sums are accumulated in float64.
+    Sums are accumulated in float64.  With ``with_abs`` a third result holds
+    the same reduction over absolute values (``sum |terms|`` per grad_W
+    element), the scale of any fp32 summation error.
     """
     x = np.asarray(x, dtype=np.float32)
     g = np.asarray(g, dtype=np.float32)
@@ -223,6 +225,14 @@ def x_ple_backward(g, x, edges, inv_w, n_bins, W, mode: str = "f32"):
         dot_prev = np.einsum("nfd,nfd->nf", g64, Wq[f_idx, km1])
         grad_x = grad_x + np.where(boundary, r_prev * dot_prev, 0.0)
 
+    grad_W = _reverse_prefix(k, tq, g64, n_bins, f, b_max, d)
+    if with_abs:
+        return grad_x, grad_W, _reverse_prefix(k, np.abs(tq), np.abs(g64), n_bins, f, b_max, d)
+    return grad_x, grad_W
+
+
+def _reverse_prefix(k, tq, g64, n_bins, f, b_max, d):
+    """``grad_W[i, phys(j)] = U[j] + sum_{j'>j} H[j']`` (zero padding rows)."""
     grad_W = np.zeros((f, b_max, d), dtype=np.float64)
     for i in range(f):
         nb = int(n_bins[i])
@@ -236,7 +246,7 @@ def x_ple_backward(g, x, edges, inv_w, n_bins, W, mode: str = "f32"):
             phys_j = b_max - 1 if j == nb - 1 else j
             grad_W[i, phys_j] = U[j] + suffix
             suffix = suffix + H[j]
-    return grad_x, grad_W
+    return grad_W
 
 
 # ---------------------------------------------------------------------------
@@ -287,17 +297,42 @@ def embeddings_backward(g, x, edges, inv_w, n_bins, W, *, version="A", activatio
                                  mode=mode)
     g_ple = g * (z > 0) if activation else g
     g_ple = g_ple.astype(np.float32)
-    grad_x, grad_W = x_ple_backward(quantize(g_ple, mode), x, edges, inv_w, n_bins, W, mode)
-    out = {"grad_W": grad_W}
+    grad_x, grad_W, abs_W = x_ple_backward(quantize(g_ple, mode), x, edges, inv_w, n_bins, W, mode,
+                                           with_abs=True)
+    out = {"grad_W": grad_W, "abs": {"grad_W": abs_W}}
     g64 = g.astype(np.float64)
     if version == "A":
         out["grad_bias"] = g_ple.astype(np.float64).sum(axis=0)
+        out["abs"]["grad_bias"] = np.abs(g_ple.astype(np.float64)).sum(axis=0)
     else:
-        out["grad_w0"] = np.einsum("nfd,nf->fd", g64, x.astype(np.float64))
+        x64 = x.astype(np.float64)
+        out["grad_w0"] = np.einsum("nfd,nf->fd", g64, x64)
         out["grad_b0"] = g64.sum(axis=0)
+        out["abs"]["grad_w0"] = np.einsum("nfd,nf->fd", np.abs(g64), np.abs(x64))
+        out["abs"]["grad_b0"] = np.abs(g64).sum(axis=0)
         grad_x = grad_x + np.einsum("nfd,fd->nf", g64, w0.astype(np.float64))
     out["grad_x"] = grad_x
     return out
+
+
+# fp32 summation allowance: any fp32 summation order of n terms differs from the
+# exact sum by up to ~n*u*sum|terms| (u = 2**-24); batch reductions are compared
+# with 2**-20 * sum|terms| added to the element tolerance.
+SUM_ALLOWANCE = 2.0 ** -20
+
+
+def assert_reduction_close(got, ref, abs_sum, rtol=1e-4, atol=1e-5, err_msg=""):
+    """Element-wise ``|got - ref| <= atol + rtol*|ref| + SUM_ALLOWANCE*sum|terms|``."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    bound = atol + rtol * np.abs(ref) + SUM_ALLOWANCE * np.asarray(abs_sum, np.float64)
+    bad = ~(np.abs(got - ref) <= bound)
+    if bad.any():
+        idx = np.argwhere(bad)[:5].tolist()
+        raise AssertionError(
+            f"{err_msg}: {int(bad.sum())} of {bad.size} elements outside the tolerance; first {idx}: "
+            f"got {got[bad][:5]}, ref {ref[bad][:5]}, bound {bound[bad][:5]}"
+        )
 
 
 # ---------------------------------------------------------------------------

@@ -10,70 +10,89 @@
 //              (+ <g, w0> for epilogue B)
 //   grad_bias = sum_b g'  (A);  grad_w0 = sum_b g x, grad_b0 = sum_b g  (B)
 //
-// Work decomposition.  A CTA owns Fc consecutive features and a contiguous
-// sample partition; W_f warps per feature.  Per tile of S_t samples:
-//   A  bin search of every (sample, feature) pair, per-(feature, quarter, bin)
-//      counts (integer shared atomics: order independent);
+// Work decomposition.  The grid is one persistent CTA per SM; CTA j owns an
+// equal contiguous range of the flattened (feature chunk, sample) space, i.e.
+// one or a few (chunk, sample range) segments.  16 warps = Fc features x Wf
+// warps.  Per segment the chunk's tables are staged and H/U zeroed; per tile
+// of S_t samples (x arrives by cp.async one tile ahead):
+//   A  bin search of every pair, per-(feature, quarter, bin) counts (integer
+//      shared atomics: order independent);
 //   B  exclusive scan of the counts (bin-major, quarter-minor);
 //   C  stable counting sort: each warp ranks its quarter with __match_any_sync,
 //      so the sorted order is a pure function of the input;
 //   D  walk: a feature's sorted list is cut into G equal contiguous segments;
-//      each lane group (nc lanes x VEC elements = one row of D) walks one
-//      segment, keeping the active bin's T/S rows and its running H/U sums in
-//      registers.  A run that starts inside the segment is flushed to the
-//      shared H/U histogram by its only owner; the segment's first run goes
-//      to a carry slot.  grad_x is reduced across the nc lanes of the row and
-//      scattered to a natural-order shared buffer;
-//   E  carries are added in segment order (deterministic), grad_x rows are
-//      stored coalesced.
-// At the end, per column, a suffix scan over bins turns H/U into grad_W;
-// per-partition partials go to the workspace and a finalize kernel sums them
-// in partition order.  No floating-point atomics anywhere: bitwise
-// deterministic for a given shape.
+//      each lane group (nc lanes x VEC elements = one D row) walks one segment
+//      four samples at a time (four gradient-row gathers in flight), keeping
+//      the active bin's T/S rows and running H/U sums in registers and
+//      flushing a run to the shared H/U histogram once, by its only owner (the
+//      segment in which it starts); a segment's first run goes to a carry
+//      slot.  grad_x is reduced across the row's lanes and scattered to a
+//      natural-order buffer;
+//   E  carries are added in segment order, grad_x rows stored coalesced.
+// At the end of a segment a suffix scan over bins turns H/U into grad_W and
+// the partial goes to the workspace; ple_bwd_finalize_kernel sums the
+// partials of each feature in CTA order.  No floating-point atomics:
+// bitwise deterministic for a given shape and device.
 #include <type_traits>
 
 #include "ple_common.cuh"
 #include "ple_internal.h"
+#include "ple_simd.cuh"
 
 namespace ple {
 
 struct BwdLayout {
-  float *sT, *sS, *sH, *sU, *sE, *sR, *sGX, *sCarry;
+  float *sT, *sS, *sH, *sU, *sE, *sR, *sGX, *sCarry, *sXb;
   int2* sEnt;
   uint8_t* sKey;
   int *sN, *sCnt, *sCarryBin;
 };
 
-__device__ __forceinline__ BwdLayout bwd_layout(unsigned char* base, const BwdArgs& a, int G) {
-  BwdLayout L;
-  const int tab = a.B * a.Fc * a.D;
-  L.sT = reinterpret_cast<float*>(base);
-  L.sS = L.sT + tab;
-  L.sH = L.sS + tab;
-  L.sU = L.sH + tab;
-  L.sCarry = L.sU + tab;                                   // [Fc][G][2][D]
-  L.sGX = L.sCarry + a.Fc * G * 2 * a.D;                   // [Fc][S_t]
-  L.sEnt = reinterpret_cast<int2*>(L.sGX + a.Fc * a.S_t);  // [Fc][S_t]
-  L.sE = reinterpret_cast<float*>(L.sEnt + a.Fc * a.S_t);  // [pow2][Fc]
-  L.sR = L.sE + a.pow2 * a.Fc;                             // [B][Fc]
-  L.sN = reinterpret_cast<int*>(L.sR + a.B * a.Fc);        // [Fc]
-  L.sCnt = L.sN + a.Fc;                                    // [Fc][B][Wf]
-  L.sCarryBin = L.sCnt + a.Fc * a.B * a.Wf;                // [Fc][G]
-  L.sKey = reinterpret_cast<uint8_t*>(L.sCarryBin + a.Fc * G);  // [Fc][S_t]
-  return L;
+struct BwdDims {
+  int Fc, Wf, S_t, G;
+};
+
+__host__ __device__ __forceinline__ size_t bwd_layout_bytes(const BwdArgs& a, const BwdDims& m, BwdLayout* L,
+                                                            unsigned char* base) {
+  const size_t tab = (size_t)a.B * m.Fc * a.D;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 15) & ~(size_t)15;
+    return base + o;
+  };
+  unsigned char* pT = take(4 * tab * 4);
+  unsigned char* pCarry = take((size_t)m.Fc * m.G * 2 * a.D * 4);
+  unsigned char* pGX = take((size_t)m.Fc * m.S_t * 4);
+  unsigned char* pEnt = take((size_t)m.Fc * m.S_t * 8);
+  unsigned char* pXb = take((size_t)2 * m.S_t * m.Fc * 4);
+  unsigned char* pE = take((size_t)a.pow2 * m.Fc * 4);
+  unsigned char* pR = take((size_t)a.B * m.Fc * 4);
+  unsigned char* pN = take((size_t)m.Fc * 4);
+  unsigned char* pCnt = take((size_t)m.Fc * a.B * m.Wf * 4);
+  unsigned char* pCB = take((size_t)m.Fc * m.G * 4);
+  unsigned char* pKey = take((size_t)m.Fc * m.S_t);
+  if (L) {
+    L->sT = reinterpret_cast<float*>(pT);
+    L->sS = L->sT + tab;
+    L->sH = L->sS + tab;
+    L->sU = L->sH + tab;
+    L->sCarry = reinterpret_cast<float*>(pCarry);
+    L->sGX = reinterpret_cast<float*>(pGX);
+    L->sEnt = reinterpret_cast<int2*>(pEnt);
+    L->sXb = reinterpret_cast<float*>(pXb);
+    L->sE = reinterpret_cast<float*>(pE);
+    L->sR = reinterpret_cast<float*>(pR);
+    L->sN = reinterpret_cast<int*>(pN);
+    L->sCnt = reinterpret_cast<int*>(pCnt);
+    L->sCarryBin = reinterpret_cast<int*>(pCB);
+    L->sKey = reinterpret_cast<uint8_t*>(pKey);
+  }
+  return off;
 }
 
-size_t bwd_smem_bytes(const BwdArgs& a, int G) {
-  const size_t tab = (size_t)a.B * a.Fc * a.D;
-  size_t f = 4 * tab + (size_t)a.Fc * G * 2 * a.D + (size_t)a.Fc * a.S_t;
-  size_t bytes = f * 4 + (size_t)a.Fc * a.S_t * 8 + (size_t)a.pow2 * a.Fc * 4 +
-                 (size_t)a.B * a.Fc * 4 + (size_t)a.Fc * 4 + (size_t)a.Fc * a.B * a.Wf * 4 +
-                 (size_t)a.Fc * G * 4 + (size_t)a.Fc * a.S_t;
-  return (bytes + 15) & ~(size_t)15;
-}
-
-// Exclusive scan of cnt[0..m) in place by one warp; returns the total.
-__device__ __forceinline__ int warp_exclusive_scan(int* cnt, int m, int lane) {
+// Exclusive scan of cnt[0..m) in place by one warp.
+__device__ __forceinline__ void warp_exclusive_scan(int* cnt, int m, int lane) {
   const int per = (m + 31) / 32;
   const int lo = min(lane * per, m), hi = min(lo + per, m);
   int local = 0;
@@ -90,107 +109,199 @@ __device__ __forceinline__ int warp_exclusive_scan(int* cnt, int m, int lane) {
     cnt[j] = run;
     run += c;
   }
-  return __shfl_sync(0xffffffffu, incl, 31);
 }
 
 // Sum over the nc lanes of a row group (lanes r*nc .. r*nc+nc-1); result in c == 0.
 __device__ __forceinline__ float row_reduce(float v, int c, int nc) {
-  for (int off = 1; off < nc; off <<= 1) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    if (off >= nc) break;
     const float o = __shfl_down_sync(0xffffffffu, v, off);
     if (c + off < nc) v += o;
   }
   return v;
 }
 
-template <typename QT, typename GT, int VEC>
-__global__ void __launch_bounds__(kBwdThreads, VEC >= 8 ? 1 : 2)
+// Raw gradient chunk of VEC elements of GT (kept packed until use).
+template <typename GT, int VEC> struct GRaw {
+  static constexpr int kWords = (int)(sizeof(GT) * VEC + 3) / 4;
+  unsigned w[kWords];
+};
+
+template <typename GT, int VEC>
+__device__ __forceinline__ void ldg_raw(GRaw<GT, VEC>& r, const GT* p) {
+  constexpr int bytes = (int)sizeof(GT) * VEC;
+  if constexpr (bytes == 32) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    r.w[0] = a.x; r.w[1] = a.y; r.w[2] = a.z; r.w[3] = a.w;
+    r.w[4] = b.x; r.w[5] = b.y; r.w[6] = b.z; r.w[7] = b.w;
+  } else if constexpr (bytes == 16) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    r.w[0] = a.x; r.w[1] = a.y; r.w[2] = a.z; r.w[3] = a.w;
+  } else if constexpr (bytes == 8) {
+    const uint2 a = __ldg(reinterpret_cast<const uint2*>(p));
+    r.w[0] = a.x; r.w[1] = a.y;
+  } else if constexpr (bytes == 4) {
+    r.w[0] = __ldg(reinterpret_cast<const unsigned*>(p));
+  } else {
+    r.w[0] = (unsigned)__ldg(reinterpret_cast<const unsigned short*>(p));
+  }
+}
+
+// Elements e, e+1 (e even) of a raw chunk as fp32.
+template <typename GT, int VEC>
+__device__ __forceinline__ void raw_pair(const GRaw<GT, VEC>& r, int e, float& lo, float& hi) {
+  if constexpr (std::is_same<GT, float>::value) {
+    lo = __uint_as_float(r.w[e]);
+    hi = __uint_as_float(r.w[e + 1]);
+  } else {
+    widen_pack<GT>(r.w[e >> 1], lo, hi);
+  }
+}
+template <typename GT, int VEC>
+__device__ __forceinline__ float raw_one(const GRaw<GT, VEC>& r) {
+  if constexpr (std::is_same<GT, float>::value) return __uint_as_float(r.w[0]);
+  else return Dt<GT>::to_f(*reinterpret_cast<const GT*>(&r.w[0]));
+}
+
+// Largest value that rounds to zero in QT: with no bias after the rounding,
+// q(p) > 0 exactly when p > threshold (ties round to the even zero).
+template <typename QT> __device__ __forceinline__ float zero_round_threshold() {
+  if constexpr (std::is_same<QT, float>::value) return 0.0f;
+  else if constexpr (std::is_same<QT, __nv_bfloat16>::value) return __uint_as_float(0x00008000u);  // 2^-134
+  else return 2.98023223876953125e-08f;                                                           // 2^-25
+}
+
+constexpr int kWalkUnroll = 4;
+
+template <typename QT, typename GT, int VEC, int EPI, bool RELU>
+__global__ void __launch_bounds__(kBwdThreads, 1)
 ple_bwd_kernel(const BwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int Fc = a.Fc, B = a.B, D = a.D, Wf = a.Wf, S_t = a.S_t;
+  const int lgFc = a.lgFc, lgWf = a.lgWf, lgSt = a.lgSt;
+  const int Fc = 1 << lgFc, Wf = 1 << lgWf, S_t = 1 << lgSt;
+  const int B = a.B, D = a.D, pow2 = a.pow2;
   const int nc = D / VEC;
   const int Rint = 32 / nc;
   const int G = Wf * Rint;
-  BwdLayout L = bwd_layout(smem_raw, a, G);
+  BwdLayout L;
+  bwd_layout_bytes(a, BwdDims{Fc, Wf, S_t, G}, &L, smem_raw);
 
-  const int chunk = blockIdx.x % a.n_chunks;
-  const int part = blockIdx.x / a.n_chunks;
-  const int f0 = chunk * Fc;
-  const int fc = min(Fc, a.F - f0);
-  const int64_t s_begin = a.N * part / a.n_parts;
-  const int64_t s_end = a.N * (part + 1) / a.n_parts;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int lane = tid & 31, wid = tid >> 5;
-  const int my_i = wid / Wf;          // feature slot of this warp
-  const int my_w = wid - my_i * Wf;   // warp rank within the feature
-  const int r = lane / nc, c = lane - (lane / nc) * nc;
-  const bool grp_live = r < Rint && my_i < fc;
-  const int g_seg = my_w * Rint + r;  // segment index within the feature
+  const int my_i = wid >> lgWf;         // feature slot of this warp
+  const int my_w = wid & (Wf - 1);      // warp rank within the feature
+  const int r = lane / nc, c = lane - r * nc;
+  const int g_seg = my_w * Rint + r;    // walk segment of this lane group
   const int cd = c * VEC;
   const bool do_gx = a.grad_x != nullptr;
   const GT* gptr = reinterpret_cast<const GT*>(a.g);
+  const int lg_q = lgSt - lgWf;         // quarter length (log2)
 
-  // ---- prologue: tables (same construction as the forward) and zeroed H/U
-  for (int i = tid; i < Fc; i += nthr) {
-    int n = i < fc ? a.n_bins[f0 + i] : 1;
-    L.sN[i] = n < 1 ? 1 : (n > B ? B : n);
-  }
-  __syncthreads();
-  for (int idx = tid; idx < a.pow2 * Fc; idx += nthr) {
-    const int j = idx / Fc, i = idx - j * Fc;
-    float e = __int_as_float(0x7f800000);
-    if (i < fc && j <= L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j];
-    L.sE[idx] = e;
-  }
-  for (int idx = tid; idx < B * Fc; idx += nthr) {
-    const int j = idx / Fc, i = idx - j * Fc;
-    L.sR[idx] = (i < fc && j < L.sN[i]) ? a.inv_w[(int64_t)(f0 + i) * B + j] : 0.0f;
-  }
-  for (int idx = tid; idx < B * Fc * D; idx += nthr) {
-    L.sH[idx] = 0.0f;
-    L.sU[idx] = 0.0f;
-    L.sS[idx] = 0.0f;
-  }
-  __syncthreads();
-  const float* Wc = a.W + (int64_t)f0 * B * D;
-  for (int idx = tid; idx < fc * B * D; idx += nthr) {
-    const int i = idx / (B * D);
-    const int rem = idx - i * B * D;
-    const int p = rem / D, d = rem - p * D;
-    const int n = L.sN[i];
-    const int lg = (p == B - 1) ? n - 1 : (p < n - 1 ? p : -1);
-    if (lg >= 0) L.sS[(lg * Fc + i) * D + d] = quantize<QT>(Wc[idx]);
-  }
-  __syncthreads();
-  for (int col = tid; col < Fc * D; col += nthr) {
-    const int i = col / D, d = col - i * D;
-    const int n = L.sN[i];
-    float acc = 0.0f;
-    for (int j = 0; j < n; ++j) {
-      const int o = (j * Fc + i) * D + d;
-      L.sT[o] = acc;
-      acc += L.sS[o];
+  // this CTA's range of the flattened (chunk, sample) space
+  const int64_t total = (int64_t)a.n_chunks * a.N;
+  int64_t u_lo = total * blockIdx.x / gridDim.x;
+  const int64_t u_hi = total * (blockIdx.x + 1) / gridDim.x;
+
+  for (int seg = 0; u_lo < u_hi; ++seg) {
+    const int chunk = (int)(u_lo / a.N);
+    const int64_t s_begin = u_lo - (int64_t)chunk * a.N;
+    const int64_t s_end = min64(a.N, s_begin + (u_hi - u_lo));
+    u_lo += s_end - s_begin;
+    const int f0 = chunk << lgFc;
+    const int fc = min(Fc, a.F - f0);
+    const bool grp_live = r < Rint && my_i < fc;
+    const bool x_vec4 = a.x_vec4 && fc == Fc;
+
+    auto load_x = [&](int64_t t0, int ns, float* dst) {
+      if (x_vec4) {
+        const int per_row = Fc >> 2;
+        for (int q = tid; q < ns * per_row; q += nthr) {
+          const int s = q / per_row, c4 = q - s * per_row;
+          cp_async16(dst + s * Fc + 4 * c4, a.x + (t0 + s) * a.F + f0 + 4 * c4);
+        }
+      } else {
+        for (int q = tid; q < (ns << lgFc); q += nthr) {
+          const int s = q >> lgFc, i = q & (Fc - 1);
+          if (i < fc) cp_async4(dst + q, a.x + (t0 + s) * a.F + f0 + i);
+          else dst[q] = 0.0f;
+        }
+      }
+      cp_async_commit();
+    };
+
+    __syncthreads();  // previous segment finished with every shared buffer
+    load_x(s_begin, (int)min64(S_t, s_end - s_begin), L.sXb);
+
+    // ---- tables (as the forward) and zeroed H/U
+    for (int i = tid; i < Fc; i += nthr) {
+      int n = i < fc ? a.n_bins[f0 + i] : 1;
+      L.sN[i] = n < 1 ? 1 : (n > B ? B : n);
     }
-  }
+    for (int idx = tid; idx < B * Fc * D; idx += nthr) {
+      L.sH[idx] = 0.0f;
+      L.sU[idx] = 0.0f;
+      L.sS[idx] = 0.0f;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < pow2 * Fc; idx += nthr) {
+      const int j = idx >> lgFc, i = idx & (Fc - 1);
+      float e = __int_as_float(0x7f800000);
+      if (i < fc && j <= L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j];
+      L.sE[idx] = e;
+    }
+    for (int idx = tid; idx < B * Fc; idx += nthr) {
+      const int j = idx >> lgFc, i = idx & (Fc - 1);
+      L.sR[idx] = (i < fc && j < L.sN[i]) ? a.inv_w[(int64_t)(f0 + i) * B + j] : 0.0f;
+    }
+    const float* Wc = a.W + (int64_t)f0 * B * D;
+    for (int idx = tid; idx < fc * B * D; idx += nthr) {
+      const int i = idx / (B * D);
+      const int rem = idx - i * B * D;
+      const int p = rem / D, d = rem - p * D;
+      const int n = L.sN[i];
+      const int lg = (p == B - 1) ? n - 1 : (p < n - 1 ? p : -1);
+      if (lg >= 0) L.sS[((lg << lgFc) + i) * D + d] = quantize<QT>(Wc[idx]);
+    }
+    __syncthreads();
+    for (int col = tid; col < Fc * D; col += nthr) {
+      const int i = col / D, d = col - i * D;
+      const int n = L.sN[i];
+      float acc = 0.0f;
+      for (int j = 0; j < n; ++j) {
+        const int o = ((j << lgFc) + i) * D + d;
+        L.sT[o] = acc;
+        acc += L.sS[o];
+      }
+    }
 
-  // per-lane epilogue parameters and linear0 accumulators
-  FV<VEC> pw0, pbias, acc_w0, acc_b0;
+    // per-lane epilogue parameters and linear0 accumulators (packed pairs)
+    constexpr int NP = VEC / 2 > 0 ? VEC / 2 : 1;
+    FV<VEC> pw0, pbias;
+    f2_t acc_w0[NP], acc_b0[NP];
+    float acc_w0_1 = 0.f, acc_b0_1 = 0.f;
 #pragma unroll
-  for (int e = 0; e < VEC; ++e) { pw0.v[e] = 0.f; pbias.v[e] = 0.f; acc_w0.v[e] = 0.f; acc_b0.v[e] = 0.f; }
-  if (grp_live) {
-    const int64_t po = (int64_t)(f0 + my_i) * D + cd;
-    if (a.epi == kEpiA) pbias = ldg_f32vec<float, VEC>(a.bias + po);
-    if (a.epi == kEpiB) pw0 = ldg_f32vec<float, VEC>(a.w0 + po);
-  }
-  __syncthreads();
+    for (int e = 0; e < VEC; ++e) { pw0.v[e] = 0.f; pbias.v[e] = 0.f; }
+#pragma unroll
+    for (int e = 0; e < NP; ++e) { acc_w0[e] = pack2(0.f, 0.f); acc_b0[e] = pack2(0.f, 0.f); }
+    if (grp_live) {
+      const int64_t po = (int64_t)(f0 + my_i) * D + cd;
+      if constexpr (EPI == kEpiA && RELU) pbias = ldg_f32vec<float, VEC>(a.bias + po);
+      if constexpr (EPI == kEpiB) pw0 = ldg_f32vec<float, VEC>(a.w0 + po);
+    }
 
-  const int n_i = grp_live ? L.sN[my_i] : 1;
-  for (int64_t t0 = s_begin; t0 < s_end; t0 += S_t) {
-    const int ns = (int)min64(S_t, s_end - t0);
-    const int qlen = (ns + Wf - 1) / Wf;
-    // prefetch the next tile's gradient rows of this chunk into L2
-    {
-      const int64_t nt0 = t0 + S_t;
-      if (nt0 < s_end) {
+    int buf = 0;
+    for (int64_t t0 = s_begin; t0 < s_end; t0 += S_t, buf ^= 1) {
+      const int ns = (int)min64(S_t, s_end - t0);
+      const float* sX = L.sXb + buf * S_t * Fc;
+      for (int idx = tid; idx < Fc * B * Wf; idx += nthr) L.sCnt[idx] = 0;
+      cp_async_wait_all();
+      __syncthreads();  // x tile landed, counts zeroed, previous tile finished
+      if (t0 + S_t < s_end) load_x(t0 + S_t, (int)min64(S_t, s_end - t0 - S_t), L.sXb + (buf ^ 1) * S_t * Fc);
+      // prefetch the next tile's gradient rows of this chunk into L2
+      if (t0 + S_t < s_end) {
+        const int64_t nt0 = t0 + S_t;
         const int nns = (int)min64(S_t, s_end - nt0);
         const int row_bytes = fc * D * (int)sizeof(GT);
         const int lines = row_bytes / 128 + 2;
@@ -201,229 +312,294 @@ ple_bwd_kernel(const BwdArgs a) {
           if (pp < rp + row_bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
         }
       }
-    }
-    // ---- A: bins, counts, natural-order x
-    for (int idx = tid; idx < Fc * B * Wf; idx += nthr) L.sCnt[idx] = 0;
-    __syncthreads();
-    for (int p = tid; p < ns * Fc; p += nthr) {
-      const int s = p / Fc, i = p - s * Fc;
-      if (i < fc) {
-        const float xv = a.x[(t0 + s) * a.F + f0 + i];
-        const int k = logical_bin(edge_count(xv, L.sE, Fc, i, a.pow2), L.sN[i]);
-        L.sKey[i * S_t + s] = (uint8_t)k;
-        L.sGX[i * S_t + s] = xv;
-        atomicAdd(&L.sCnt[(i * B + k) * Wf + s / qlen], 1);
-      }
-    }
-    __syncthreads();
-    // ---- B: exclusive scan per feature (bin-major, quarter-minor)
-    for (int i = wid; i < fc; i += nthr / 32) warp_exclusive_scan(L.sCnt + i * B * Wf, B * Wf, lane);
-    __syncthreads();
-    // ---- C: stable scatter of each quarter into sorted order
-    if (my_i < fc) {
-      const int q = my_w;
-      const int lo = q * qlen, hi = min(lo + qlen, ns);
-      for (int base = lo; base < hi; base += 32) {
-        const int s = base + lane;
-        const bool v = s < hi;
-        const unsigned act = __ballot_sync(0xffffffffu, v);
-        if (v) {
-          const int k = L.sKey[my_i * S_t + s];
-          const unsigned peers = __match_any_sync(act, k);
-          const int leader = __ffs(peers) - 1;
-          const int rank = __popc(peers & ((1u << lane) - 1u));
-          int* cur = &L.sCnt[(my_i * B + k) * Wf + q];
-          int pos0 = 0;
-          if (lane == leader) pos0 = *cur;
-          pos0 = __shfl_sync(peers, pos0, leader);
-          if (lane == leader) *cur = pos0 + __popc(peers);
-          const float xv = L.sGX[my_i * S_t + s];
-          L.sEnt[my_i * S_t + pos0 + rank] = make_int2(__float_as_int(xv), s | (k << 16));
+      // ---- A: bins and counts
+      for (int p = tid; p < (ns << lgFc); p += nthr) {
+        const int s = p >> lgFc, i = p & (Fc - 1);
+        if (i < fc) {
+          const float xv = sX[p];
+          const int k = logical_bin(edge_count(xv, L.sE, Fc, i, pow2), L.sN[i]);
+          L.sKey[(i << lgSt) + s] = (uint8_t)k;
+          atomicAdd(&L.sCnt[((i * B + k) << lgWf) + (s >> lg_q)], 1);
         }
-        __syncwarp();
       }
-    }
-    __syncthreads();
-    // ---- D: segmented walk
-    if (my_i < fc) {
-      const int seg_lo = (int)((int64_t)g_seg * ns / G);
-      const int seg_hi = (int)((int64_t)(g_seg + 1) * ns / G);
-      const int my_len = grp_live ? seg_hi - seg_lo : 0;
-      // uniform trip count for the warp (segments differ by at most one)
-      int trips = my_len;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) trips = max(trips, __shfl_xor_sync(0xffffffffu, trips, off));
-      int k_cur = -1;
-      bool first_run = true;
-      float e_k = 0.f, r_k = 0.f, r_km1 = 0.f;
-      FV<VEC> Tk, Sk, Skm1, Hrun, Urun;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) { Tk.v[e] = Sk.v[e] = Skm1.v[e] = Hrun.v[e] = Urun.v[e] = 0.f; }
-      float* carry = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
-      if (grp_live && c == 0) L.sCarryBin[my_i * G + g_seg] = -1;
-      for (int step = 0; step < trips; ++step) {
-        const bool live = step < my_len;
-        int2 ent = make_int2(0, 0);
-        int k = k_cur;
-        if (live) {
-          ent = L.sEnt[my_i * S_t + seg_lo + step];
-          k = ent.y >> 16;
-        }
-        if (live && k != k_cur) {
-          if (k_cur >= 0) {
-            if (first_run) {
-              sts<VEC>(carry, Hrun);
-              sts<VEC>(carry + D, Urun);
-              if (c == 0) L.sCarryBin[my_i * G + g_seg] = k_cur;
-            } else {
-              float* h = L.sH + (k_cur * Fc + my_i) * D + cd;
-              float* u = L.sU + (k_cur * Fc + my_i) * D + cd;
-              FV<VEC> hv = lds<VEC>(h), uv = lds<VEC>(u);
-#pragma unroll
-              for (int e = 0; e < VEC; ++e) { hv.v[e] += Hrun.v[e]; uv.v[e] += Urun.v[e]; }
-              sts<VEC>(h, hv);
-              sts<VEC>(u, uv);
-            }
-            first_run = false;
+      __syncthreads();
+      // ---- B: exclusive scan per feature (bin-major, quarter-minor)
+      for (int i = wid; i < fc; i += nthr / 32) warp_exclusive_scan(L.sCnt + ((i * B) << lgWf), B << lgWf, lane);
+      __syncthreads();
+      // ---- C: stable scatter of each quarter into sorted order
+      if (my_i < fc) {
+        const int lo = my_w << lg_q, hi = min(lo + (1 << lg_q), ns);
+        for (int base = lo; base < hi; base += 32) {
+          const int s = base + lane;
+          const bool v = s < hi;
+          const unsigned act = __ballot_sync(0xffffffffu, v);
+          if (v) {
+            const int k = L.sKey[(my_i << lgSt) + s];
+            const unsigned peers = __match_any_sync(act, k);
+            const int leader = __ffs(peers) - 1;
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            int* cur = &L.sCnt[((my_i * B + k) << lgWf) + my_w];
+            int pos0 = 0;
+            if (lane == leader) pos0 = *cur;
+            pos0 = __shfl_sync(peers, pos0, leader);
+            if (lane == leader) *cur = pos0 + __popc(peers);
+            const float xv = sX[(s << lgFc) + my_i];
+            L.sEnt[(my_i << lgSt) + pos0 + rank] = make_int2(__float_as_int(xv), s | (k << 16));
           }
-          k_cur = k;
-          const int to = (k * Fc + my_i) * D + cd;
-          Tk = lds<VEC>(L.sT + to);
-          Sk = lds<VEC>(L.sS + to);
-          e_k = L.sE[k * Fc + my_i];
-          r_k = L.sR[k * Fc + my_i];
-          if (k > 0) {
-            Skm1 = lds<VEC>(L.sS + to - Fc * D);
-            r_km1 = L.sR[(k - 1) * Fc + my_i];
-          }
+          __syncwarp();
+        }
+      }
+      __syncthreads();
+      // ---- D: segmented walk
+      if (my_i < fc) {
+        const int seg_lo = (int)(((int64_t)g_seg * ns) / G);
+        const int seg_hi = (int)(((int64_t)(g_seg + 1) * ns) / G);
+        const int my_len = grp_live ? seg_hi - seg_lo : 0;
+        int trips = my_len;
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) { Hrun.v[e] = 0.f; Urun.v[e] = 0.f; }
-        }
-        float gx = 0.f;
-        int s = 0;
-        if (live) {
-          const float xv = __int_as_float(ent.x);
-          s = ent.y & 0xffff;
-          const float t = (xv - e_k) * r_k;
-          const float tq = quantize<QT>(t);
-          const bool edge_tie = (k > 0) && (xv == e_k);
-          const FV<VEC> gv = ldg_vec<GT, VEC>(gptr + ((t0 + s) * a.F + f0 + my_i) * D + cd);
-          float dot = 0.f, dot_prev = 0.f, dot_w0 = 0.f;
+        for (int off = 16; off > 0; off >>= 1) trips = max(trips, __shfl_xor_sync(0xffffffffu, trips, off));
+        int k_cur = -1;
+        bool first_run = true;
+        float e_k = 0.f, r_k = 0.f, r_km1 = 0.f;
+        FV<VEC> Tk, Sk, Skm1, Hrun, Urun;
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            float gp = gv.v[e];
-            if (a.relu) {
-              float z = quantize<QT>(fmaf(tq, Sk.v[e], Tk.v[e]));
-              if (a.epi == kEpiA) z += pbias.v[e];
-              gp = z > 0.0f ? gp : 0.0f;
-            }
-            float gq = gp;
-            if constexpr (!std::is_same<GT, QT>::value) gq = quantize<QT>(gp);
-            Hrun.v[e] += gq;
-            Urun.v[e] = fmaf(tq, gq, Urun.v[e]);
-            dot = fmaf(gq, Sk.v[e], dot);
-            dot_prev = fmaf(gq, Skm1.v[e], dot_prev);
-            if (a.epi == kEpiB) {
-              acc_w0.v[e] = fmaf(gv.v[e], xv, acc_w0.v[e]);
-              acc_b0.v[e] += gv.v[e];
-              dot_w0 = fmaf(gv.v[e], pw0.v[e], dot_w0);
-            }
-          }
-          gx = r_k * dot + (edge_tie ? r_km1 * dot_prev : 0.f) + dot_w0;
-        }
-        if (do_gx) {
-          gx = row_reduce(gx, c, nc);
-          if (live && c == 0) L.sGX[my_i * S_t + s] = gx;
-        }
-      }
-      // flush the segment's last run
-      if (grp_live && k_cur >= 0) {
-        if (first_run) {
-          sts<VEC>(carry, Hrun);
-          sts<VEC>(carry + D, Urun);
-          if (c == 0) L.sCarryBin[my_i * G + g_seg] = k_cur;
-        } else {
-          float* h = L.sH + (k_cur * Fc + my_i) * D + cd;
-          float* u = L.sU + (k_cur * Fc + my_i) * D + cd;
-          FV<VEC> hv = lds<VEC>(h), uv = lds<VEC>(u);
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) { hv.v[e] += Hrun.v[e]; uv.v[e] += Urun.v[e]; }
-          sts<VEC>(h, hv);
-          sts<VEC>(u, uv);
-        }
-      }
-    }
-    __syncthreads();
-    // ---- E: carries in segment order; grad_x rows
-    for (int colx = tid; colx < fc * D; colx += nthr) {
-      const int i = colx / D, d = colx - i * D;
-      for (int g = 0; g < G; ++g) {
-        const int kb = L.sCarryBin[i * G + g];
-        if (kb >= 0) {
-          const float* cp = L.sCarry + ((i * G + g) * 2) * D + d;
-          L.sH[(kb * Fc + i) * D + d] += cp[0];
-          L.sU[(kb * Fc + i) * D + d] += cp[D];
-        }
-      }
-    }
-    if (do_gx) {
-      for (int p = tid; p < ns * Fc; p += nthr) {
-        const int s = p / Fc, i = p - s * Fc;
-        if (i < fc) a.grad_x[(t0 + s) * a.F + f0 + i] = L.sGX[i * S_t + s];
-      }
-    }
-    __syncthreads();
-  }
+        for (int e = 0; e < VEC; ++e) { Tk.v[e] = Sk.v[e] = Skm1.v[e] = Hrun.v[e] = Urun.v[e] = 0.f; }
+        float* carry = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
+        if (grp_live && c == 0) L.sCarryBin[my_i * G + g_seg] = -1;
+        const int2* ents = L.sEnt + (my_i << lgSt) + seg_lo;
+        const GT* grow = gptr + (t0 * a.F + f0 + my_i) * (int64_t)D + cd;
+        const int64_t gstride = (int64_t)a.F * D;
 
-  // ---- F: linear0 partials (fixed segment order) and grad_W suffix scan
-  float* ws = a.ws + (int64_t)part * a.F * (B + 3) * D;
-  if (a.epi == kEpiB) {
-    if (grp_live) {
-      float* cp = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
-      sts<VEC>(cp, acc_w0);
-      sts<VEC>(cp + D, acc_b0);
+        auto flush = [&]() {
+          if (first_run) {
+            sts<VEC>(carry, Hrun);
+            sts<VEC>(carry + D, Urun);
+            if (c == 0) L.sCarryBin[my_i * G + g_seg] = k_cur;
+            first_run = false;
+          } else {
+            float* h = L.sH + ((k_cur << lgFc) + my_i) * D + cd;
+            float* u = L.sU + ((k_cur << lgFc) + my_i) * D + cd;
+            FV<VEC> hv = lds<VEC>(h), uv = lds<VEC>(u);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) { hv.v[e] += Hrun.v[e]; uv.v[e] += Urun.v[e]; }
+            sts<VEC>(h, hv);
+            sts<VEC>(u, uv);
+          }
+        };
+
+        for (int base = 0; base < trips; base += kWalkUnroll) {
+          int2 ent[kWalkUnroll];
+          GRaw<GT, VEC> graw[kWalkUnroll];
+#pragma unroll
+          for (int u = 0; u < kWalkUnroll; ++u) {
+            const int step = base + u;
+            ent[u] = make_int2(0, -1);
+#pragma unroll
+            for (int w = 0; w < GRaw<GT, VEC>::kWords; ++w) graw[u].w[w] = 0u;
+            if (step < my_len) {
+              ent[u] = ents[step];
+              ldg_raw<GT, VEC>(graw[u], grow + (int64_t)(ent[u].y & 0xffff) * gstride);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kWalkUnroll; ++u) {
+            const bool live = base + u < my_len;
+            const int k = ent[u].y >> 16;
+            if (live && k != k_cur) {
+              if (k_cur >= 0) flush();
+              k_cur = k;
+              const int to = ((k << lgFc) + my_i) * D + cd;
+              Tk = lds<VEC>(L.sT + to);
+              Sk = lds<VEC>(L.sS + to);
+              e_k = L.sE[(k << lgFc) + my_i];
+              r_k = L.sR[(k << lgFc) + my_i];
+              if (k > 0) {
+                Skm1 = lds<VEC>(L.sS + to - (D << lgFc));
+                r_km1 = L.sR[((k - 1) << lgFc) + my_i];
+              }
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) { Hrun.v[e] = 0.f; Urun.v[e] = 0.f; }
+            }
+            float gx = 0.f;
+            if (live) {
+              const float xv = __int_as_float(ent[u].x);
+              const float t = (xv - e_k) * r_k;
+              const float tq = quantize<QT>(t);
+              const bool edge_tie = (k > 0) && (xv == e_k);
+              float dot = 0.f, dot_prev = 0.f, dot_w0 = 0.f;
+              if constexpr (VEC >= 2) {
+                const f2_t t2 = pack2(tq, tq);
+                const f2_t x2 = pack2(xv, xv);
+                f2_t d2 = pack2(0.f, 0.f), dp2 = pack2(0.f, 0.f), dw2 = pack2(0.f, 0.f);
+#pragma unroll
+                for (int e = 0; e < VEC; e += 2) {
+                  float g0, g1;
+                  raw_pair<GT, VEC>(graw[u], e, g0, g1);
+                  float q0 = g0, q1 = g1;
+                  if constexpr (RELU) {
+                    float p0, p1;
+                    unpack2(fma2(t2, pack2(Sk.v[e], Sk.v[e + 1]), pack2(Tk.v[e], Tk.v[e + 1])), p0, p1);
+                    if constexpr (EPI == kEpiA) {
+                      round2<QT>(p0, p1);
+                      p0 += pbias.v[e];
+                      p1 += pbias.v[e + 1];
+                      q0 = p0 > 0.f ? g0 : 0.f;
+                      q1 = p1 > 0.f ? g1 : 0.f;
+                    } else {
+                      const float thr = zero_round_threshold<QT>();
+                      q0 = p0 > thr ? g0 : 0.f;
+                      q1 = p1 > thr ? g1 : 0.f;
+                    }
+                  }
+                  if constexpr (!std::is_same<GT, QT>::value && !std::is_same<QT, float>::value) round2<QT>(q0, q1);
+                  const f2_t q2 = pack2(q0, q1);
+                  const f2_t h2 = add2(pack2(Hrun.v[e], Hrun.v[e + 1]), q2);
+                  const f2_t u2 = fma2(t2, q2, pack2(Urun.v[e], Urun.v[e + 1]));
+                  unpack2(h2, Hrun.v[e], Hrun.v[e + 1]);
+                  unpack2(u2, Urun.v[e], Urun.v[e + 1]);
+                  d2 = fma2(q2, pack2(Sk.v[e], Sk.v[e + 1]), d2);
+                  dp2 = fma2(q2, pack2(Skm1.v[e], Skm1.v[e + 1]), dp2);
+                  if constexpr (EPI == kEpiB) {
+                    const f2_t gg = pack2(g0, g1);
+                    acc_w0[e >> 1] = fma2(gg, x2, acc_w0[e >> 1]);
+                    acc_b0[e >> 1] = add2(acc_b0[e >> 1], gg);
+                    dw2 = fma2(gg, pack2(pw0.v[e], pw0.v[e + 1]), dw2);
+                  }
+                }
+                float lo, hi;
+                unpack2(d2, lo, hi);
+                dot = lo + hi;
+                unpack2(dp2, lo, hi);
+                dot_prev = lo + hi;
+                unpack2(dw2, lo, hi);
+                dot_w0 = lo + hi;
+              } else {
+                const float g0 = raw_one<GT, VEC>(graw[u]);
+                float q0 = g0;
+                if constexpr (RELU) {
+                  float p0 = fmaf(tq, Sk.v[0], Tk.v[0]);
+                  if constexpr (EPI == kEpiA) {
+                    p0 = quantize<QT>(p0) + pbias.v[0];
+                    q0 = p0 > 0.f ? g0 : 0.f;
+                  } else {
+                    q0 = p0 > zero_round_threshold<QT>() ? g0 : 0.f;
+                  }
+                }
+                if constexpr (!std::is_same<GT, QT>::value) q0 = quantize<QT>(q0);
+                Hrun.v[0] += q0;
+                Urun.v[0] = fmaf(tq, q0, Urun.v[0]);
+                dot = q0 * Sk.v[0];
+                dot_prev = q0 * Skm1.v[0];
+                if constexpr (EPI == kEpiB) {
+                  acc_w0_1 = fmaf(g0, xv, acc_w0_1);
+                  acc_b0_1 += g0;
+                  dot_w0 = g0 * pw0.v[0];
+                }
+              }
+              gx = r_k * dot + (edge_tie ? r_km1 * dot_prev : 0.f) + dot_w0;
+            }
+            if (do_gx) {
+              gx = row_reduce(gx, c, nc);
+              if (live && c == 0) L.sGX[(my_i << lgSt) + (ent[u].y & 0xffff)] = gx;
+            }
+          }
+        }
+        if (grp_live && k_cur >= 0) flush();
+      }
+      __syncthreads();
+      // ---- E: carries in segment order; grad_x rows
+      for (int colx = tid; colx < fc * D; colx += nthr) {
+        const int i = colx / D, d = colx - i * D;
+        for (int g = 0; g < G; ++g) {
+          const int kb = L.sCarryBin[i * G + g];
+          if (kb >= 0) {
+            const float* cp = L.sCarry + ((i * G + g) * 2) * D + d;
+            L.sH[((kb << lgFc) + i) * D + d] += cp[0];
+            L.sU[((kb << lgFc) + i) * D + d] += cp[D];
+          }
+        }
+      }
+      if (do_gx) {
+        for (int p = tid; p < (ns << lgFc); p += nthr) {
+          const int s = p >> lgFc, i = p & (Fc - 1);
+          if (i < fc) a.grad_x[(t0 + s) * a.F + f0 + i] = L.sGX[(i << lgSt) + s];
+        }
+      }
     }
+
+    // ---- F: linear0 partials (fixed segment order) and grad_W suffix scan
     __syncthreads();
+    float* ws = a.ws + ((int64_t)blockIdx.x * a.max_segs + seg) * ((int64_t)Fc * (B + 3) * D);
+    if constexpr (EPI == kEpiB) {
+      if (grp_live) {
+        float* cp = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
+        if constexpr (VEC >= 2) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 2) {
+            unpack2(acc_w0[e >> 1], cp[e], cp[e + 1]);
+            unpack2(acc_b0[e >> 1], cp[D + e], cp[D + e + 1]);
+          }
+        } else {
+          cp[0] = acc_w0_1;
+          cp[D] = acc_b0_1;
+        }
+      }
+      __syncthreads();
+      for (int colx = tid; colx < fc * D; colx += nthr) {
+        const int i = colx / D, d = colx - i * D;
+        float sw = 0.f, sb = 0.f;
+        for (int g = 0; g < G; ++g) {
+          const float* cp = L.sCarry + ((i * G + g) * 2) * D + d;
+          sw += cp[0];
+          sb += cp[D];
+        }
+        float* row = ws + (int64_t)i * (B + 3) * D;
+        row[(B + 1) * D + d] = sw;
+        row[(B + 2) * D + d] = sb;
+      }
+    }
     for (int colx = tid; colx < fc * D; colx += nthr) {
       const int i = colx / D, d = colx - i * D;
-      float sw = 0.f, sb = 0.f;
-      for (int g = 0; g < G; ++g) {
-        const float* cp = L.sCarry + ((i * G + g) * 2) * D + d;
-        sw += cp[0];
-        sb += cp[D];
+      const int n = L.sN[i];
+      float* row = ws + (int64_t)i * (B + 3) * D;
+      float suffix = 0.f;
+      for (int j = n - 1; j >= 0; --j) {
+        const int o = ((j << lgFc) + i) * D + d;
+        row[physical_bin(j, n, B) * D + d] = L.sU[o] + suffix;
+        suffix += L.sH[o];
       }
-      float* row = ws + (int64_t)(f0 + i) * (B + 3) * D;
-      row[(B + 1) * D + d] = sw;
-      row[(B + 2) * D + d] = sb;
+      for (int p = n - 1; p < B - 1; ++p) row[p * D + d] = 0.f;  // padding rows
+      row[B * D + d] = suffix;                                    // sum_b g' (bias grad)
     }
   }
-  for (int colx = tid; colx < fc * D; colx += nthr) {
-    const int i = colx / D, d = colx - i * D;
-    const int n = L.sN[i];
-    float* row = ws + (int64_t)(f0 + i) * (B + 3) * D;
-    float suffix = 0.f;
-    for (int j = n - 1; j >= 0; --j) {
-      const int o = (j * Fc + i) * D + d;
-      const int phys = physical_bin(j, n, B);
-      row[phys * D + d] = L.sU[o] + suffix;
-      suffix += L.sH[o];
-    }
-    for (int p = n - 1; p < B - 1; ++p) row[p * D + d] = 0.f;  // padding rows
-    row[B * D + d] = suffix;                                    // sum_b g' (bias grad)
-  }
-  (void)n_i;
 }
 
-// Sum the per-partition partials in partition order.
-__global__ void ple_bwd_finalize_kernel(const BwdArgs a) {
-  const int B = a.B, D = a.D;
+// Sum, per feature, the partials of the CTAs whose ranges cover its chunk, in
+// CTA order (deterministic).
+__global__ void ple_bwd_finalize_kernel(const BwdArgs a, int grid) {
+  const int B = a.B, D = a.D, lgFc = a.lgFc, Fc = 1 << lgFc;
   const int64_t rows = (int64_t)a.F * (B + 3) * D;
+  const int64_t total = (int64_t)a.n_chunks * a.N;
+  const int64_t slot = (int64_t)Fc * (B + 3) * D;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int p = 0; p < a.n_parts; ++p) s += a.ws[p * rows + idx];
     const int64_t f = idx / ((int64_t)(B + 3) * D);
     const int64_t rem = idx - f * (B + 3) * D;
+    const int chunk = (int)(f >> lgFc), i = (int)(f & (Fc - 1));
+    const int64_t c_lo = (int64_t)chunk * a.N, c_hi = c_lo + a.N;
+    // first CTA whose range [total*j/grid, total*(j+1)/grid) ends past the chunk start
+    int64_t j = c_lo * grid / total;
+    while (j > 0 && total * j / grid > c_lo) --j;
+    while (j < grid && total * (j + 1) / grid <= c_lo) ++j;
+    float s = 0.f;
+    for (; j < grid; ++j) {
+      const int64_t lo = total * j / grid;
+      const int64_t hi = total * (j + 1) / grid;
+      if (lo >= c_hi) break;
+      if (hi <= lo) continue;
+      const int seg = chunk - (int)(lo / a.N);  // segments of CTA j are consecutive chunks
+      s += a.ws[(j * a.max_segs + seg) * slot + (int64_t)i * (B + 3) * D + rem];
+    }
     const int row = (int)(rem / D), d = (int)(rem - (int64_t)row * D);
     if (row < B) {
       if (a.grad_W) a.grad_W[(f * B + row) * D + d] = s;
@@ -437,104 +613,125 @@ __global__ void ple_bwd_finalize_kernel(const BwdArgs a) {
   }
 }
 
-// ------------------------------------------------------------------ launch
-// Chunk / tile plan: 16 warps per CTA split as Fc features x Wf warps; the
-// largest tile whose shared memory allows two resident CTAs (one CTA when the
-// tables alone are too large).  Shared by the workspace query and the launch.
-static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out, int* ctas_per_sm) {
+// ------------------------------------------------------------------ planning
+// Chunk width of the walk: 8 elements for 16-bit gradients (16-byte rows),
+// 4 for fp32 unless D is large (a row group must fit in a warp).
+int backward_vec(int64_t D, int gbytes) {
+  int v = D % 8 == 0 ? 8 : (D % 4 == 0 ? 4 : (D % 2 == 0 ? 2 : 1));
+  if (gbytes == 4 && v == 8 && D <= 32) v = 4;
+  return v;
+}
+
+// Features per CTA (power of two), tile length and the layout size; false if
+// even one feature does not fit.
+static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
   const int nc = a.D / vec;
-  const int G_per_warp = 32 / nc;
+  if (nc > 32) return false;
   int pow2 = 1;
   while (pow2 < a.B + 1) pow2 <<= 1;
   a.pow2 = pow2;
   const size_t optin = device_max_smem_optin();
-  for (int want = 2; want >= 1; --want) {
-    const size_t budget = want == 2 ? kBwdSmemTwoCtas : optin;
-    for (int Fc = 4; Fc >= 1; Fc >>= 1) {
-      if (Fc / 2 >= a.F && Fc > 1) continue;
-      for (int S_t = kBwdTile; S_t >= 128; S_t >>= 1) {
-        a.Fc = Fc;
-        a.Wf = kBwdThreads / 32 / Fc;
-        a.S_t = S_t;
-        const size_t smem = bwd_smem_bytes(a, a.Wf * G_per_warp);
-        if (smem <= budget) {
-          *smem_out = smem;
-          *ctas_per_sm = want;
-          a.n_chunks = (int)ceil_div<int64_t>(a.F, a.Fc);
-          int64_t parts = (int64_t)device_sm_count() * want / a.n_chunks;
-          const int64_t max_by_n = ceil_div<int64_t>(a.N, 64);
-          parts = parts < 1 ? 1 : parts;
-          parts = parts > max_by_n ? max_by_n : parts;
-          a.n_parts = (int)parts;
-          return true;
-        }
+  for (int lgFc = 2; lgFc >= 0; --lgFc) {
+    if (lgFc > 0 && (1 << (lgFc - 1)) >= a.F) continue;
+    const int Fc = 1 << lgFc;
+    const int lgWf = 4 - lgFc;  // 16 warps
+    const int G = (1 << lgWf) * (32 / nc);
+    for (int lgSt = 10; lgSt >= 7; --lgSt) {
+      BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G};
+      const size_t bytes = bwd_layout_bytes(a, m, nullptr, nullptr);
+      if (bytes <= optin) {
+        a.lgFc = lgFc;
+        a.lgWf = lgWf;
+        a.lgSt = lgSt;
+        a.n_chunks = (int)ceil_div<int64_t>(a.F, Fc);
+        *smem_out = bytes;
+        return true;
       }
     }
   }
   return false;
 }
 
-int backward_vec(int64_t D);
-
-size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
-  BwdArgs a{};
-  a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D;
-  size_t smem = 0;
-  int per = 0;
-  if (!bwd_plan(a, backward_vec(D), &smem, &per)) return 0;
-  return (size_t)a.n_parts * (size_t)F * (size_t)(B + 3) * (size_t)D * sizeof(float);
+static void bwd_grid(BwdArgs& a, int* grid) {
+  const int64_t total = (int64_t)a.n_chunks * a.N;
+  int64_t g = device_sm_count();
+  const int64_t min_units = 64;  // at least 64 (chunk, sample) rows per CTA
+  if (g > total / min_units) g = total / min_units;
+  if (g < 1) g = 1;
+  *grid = (int)g;
+  const int64_t len = ceil_div<int64_t>(total, g);
+  a.max_segs = (int)(ceil_div<int64_t>(len, a.N) + 1);  // chunks one range can touch
 }
 
-template <typename QT, typename GT, int VEC>
+size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
+  size_t best = 0;
+  for (int gbytes : {2, 4}) {  // large enough for either gradient width
+    BwdArgs b{};
+    b.N = N; b.F = (int)F; b.B = (int)B; b.D = (int)D;
+    size_t smem = 0;
+    if (!bwd_plan(b, backward_vec(D, gbytes), &smem)) continue;
+    int grid = 0;
+    bwd_grid(b, &grid);
+    const size_t bytes = (size_t)grid * b.max_segs * ((size_t)(1 << b.lgFc) * (B + 3) * D) * sizeof(float);
+    if (bytes > best) best = bytes;
+  }
+  return best;
+}
+
+template <typename QT, typename GT, int VEC, int EPI, bool RELU>
 static int launch_bwd_t(BwdArgs a, cudaStream_t st) {
   size_t smem = 0;
-  int want = 0;
-  if (!bwd_plan(a, VEC, &smem, &want))
+  if (!bwd_plan(a, VEC, &smem))
     return set_error(PLE_ERR_UNSUPPORTED, "backward: tables do not fit in shared memory");
-  auto kern = ple_bwd_kernel<QT, GT, VEC>;
+  int grid = 0;
+  bwd_grid(a, &grid);
+  const size_t need = (size_t)grid * a.max_segs * ((size_t)(1 << a.lgFc) * (a.B + 3) * a.D) * sizeof(float);
+  if (need > a.ws_bytes)
+    return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
+  a.x_vec4 = ((1 << a.lgFc) >= 4) && (a.F % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+  auto kern = ple_bwd_kernel<QT, GT, VEC, EPI, RELU>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kBwdThreads, smem);
-  if (e != cudaSuccess) return set_cuda_error(e, "occupancy(backward)");
-  if (per_sm < 1) return set_error(PLE_ERR_UNSUPPORTED, "backward: no resident CTA fits");
-  if (per_sm < want) {
-    // fewer resident CTAs than planned (registers): shrink the partition count
-    int64_t parts = (int64_t)device_sm_count() * per_sm / a.n_chunks;
-    a.n_parts = (int)(parts < 1 ? 1 : (parts < a.n_parts ? parts : a.n_parts));
-  }
-  if ((size_t)a.n_parts * a.F * (a.B + 3) * a.D * sizeof(float) > a.ws_bytes)
-    return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
-  const int64_t grid = (int64_t)a.n_chunks * a.n_parts;
-  if (grid > 0x7fffffff) return set_error(PLE_ERR_OVERFLOW, "backward grid too large");
-  kern<<<(unsigned)grid, kBwdThreads, smem, st>>>(a);
+  kern<<<grid, kBwdThreads, smem, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward launch");
   const int64_t rows = (int64_t)a.F * (a.B + 3) * a.D;
   const int fin_blocks = (int)min64(ceil_div<int64_t>(rows, 256), 4L * device_sm_count());
-  ple_bwd_finalize_kernel<<<fin_blocks, 256, 0, st>>>(a);
+  ple_bwd_finalize_kernel<<<fin_blocks, 256, 0, st>>>(a, grid);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward finalize launch");
   return PLE_OK;
 }
 
+template <typename QT, typename GT, int VEC>
+static int launch_bwd_epi(const BwdArgs& a, cudaStream_t st) {
+  if (a.epi == kEpiB)
+    return a.relu ? launch_bwd_t<QT, GT, VEC, kEpiB, true>(a, st) : launch_bwd_t<QT, GT, VEC, kEpiB, false>(a, st);
+  if (a.epi == kEpiA)
+    return a.relu ? launch_bwd_t<QT, GT, VEC, kEpiA, true>(a, st) : launch_bwd_t<QT, GT, VEC, kEpiA, false>(a, st);
+  return launch_bwd_t<QT, GT, VEC, kEpiNone, false>(a, st);
+}
+
 template <typename QT, typename GT>
 static int launch_bwd_vec(const BwdArgs& a, int vec, cudaStream_t st) {
   switch (vec) {
-    case 8: return launch_bwd_t<QT, GT, 8>(a, st);
-    case 4: return launch_bwd_t<QT, GT, 4>(a, st);
-    case 2: return launch_bwd_t<QT, GT, 2>(a, st);
-    default: return launch_bwd_t<QT, GT, 1>(a, st);
+    case 8: return launch_bwd_epi<QT, GT, 8>(a, st);
+    case 4: return launch_bwd_epi<QT, GT, 4>(a, st);
+    case 2: return launch_bwd_epi<QT, GT, 2>(a, st);
+    default: return launch_bwd_epi<QT, GT, 1>(a, st);
   }
 }
 
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st) {
+  (void)vec;
   const int q = compute_dtype, g = grad_dtype;
-  if (q == PLE_DTYPE_F32 && g == PLE_DTYPE_F32) return launch_bwd_vec<float, float>(a, vec, st);
-  if (q == PLE_DTYPE_BF16 && g == PLE_DTYPE_BF16) return launch_bwd_vec<__nv_bfloat16, __nv_bfloat16>(a, vec, st);
-  if (q == PLE_DTYPE_BF16 && g == PLE_DTYPE_F32) return launch_bwd_vec<__nv_bfloat16, float>(a, vec, st);
-  if (q == PLE_DTYPE_F16 && g == PLE_DTYPE_F16) return launch_bwd_vec<__half, __half>(a, vec, st);
-  if (q == PLE_DTYPE_F16 && g == PLE_DTYPE_F32) return launch_bwd_vec<__half, float>(a, vec, st);
+  const int v = backward_vec(a.D, g == PLE_DTYPE_F32 ? 4 : 2);
+  if (a.epi == kEpiNone) a.relu = 0;
+  if (q == PLE_DTYPE_F32 && g == PLE_DTYPE_F32) return launch_bwd_vec<float, float>(a, v, st);
+  if (q == PLE_DTYPE_BF16 && g == PLE_DTYPE_BF16) return launch_bwd_vec<__nv_bfloat16, __nv_bfloat16>(a, v, st);
+  if (q == PLE_DTYPE_BF16 && g == PLE_DTYPE_F32) return launch_bwd_vec<__nv_bfloat16, float>(a, v, st);
+  if (q == PLE_DTYPE_F16 && g == PLE_DTYPE_F16) return launch_bwd_vec<__half, __half>(a, v, st);
+  if (q == PLE_DTYPE_F16 && g == PLE_DTYPE_F32) return launch_bwd_vec<__half, float>(a, v, st);
   return set_error(PLE_ERR_UNSUPPORTED, "backward: unsupported (compute, grad) dtype pair");
 }
 

@@ -93,13 +93,6 @@ int pick_vec(int64_t D, int max_vec, std::initializer_list<std::pair<const void*
 int device_sm_count() { return props().sms; }
 size_t device_max_smem_optin() { return props().smem_optin; }
 
-int backward_vec(int64_t D) {
-  if (D % 8 == 0 && D >= 48) return 8;
-  if (D % 4 == 0) return 4;
-  if (D % 2 == 0) return 2;
-  return 1;
-}
-
 }  // namespace ple
 
 using namespace ple;
@@ -215,7 +208,7 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
   if (!g || !x) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad_output and x are required");
   if (!ws) return set_error(PLE_ERR_WORKSPACE, "backward needs a workspace (ple_backward_workspace_size)");
   if (!aligned(ws, 16)) return set_error(PLE_ERR_WORKSPACE, "workspace must be 16-byte aligned");
-  const int vec = backward_vec(D);
+  const int vec = backward_vec(D, dtype_size(grad_dtype));
   if (D / vec > 32) return set_error(PLE_ERR_UNSUPPORTED, "backward: odd d_embedding above 32 is not supported");
   if (!aligned(g, (size_t)vec * dtype_size(grad_dtype)) || !aligned(w0, (size_t)vec * 4) ||
       !aligned(bias, (size_t)vec * 4))

@@ -11,10 +11,8 @@ namespace ple {
 
 enum { kEpiNone = PLE_EPILOGUE_NONE, kEpiA = PLE_EPILOGUE_A, kEpiB = PLE_EPILOGUE_B };
 
-// backward tuning
+// backward tuning: 16 warps, one persistent CTA per SM
 constexpr int kBwdThreads = 512;
-constexpr int kBwdTile = 1024;
-constexpr size_t kBwdSmemTwoCtas = 112 * 1024;
 
 // forward tuning
 constexpr int kFwdMaxThreads = 256;
@@ -37,7 +35,7 @@ struct FwdArgs {
   int F, B, D;
   int epi, relu;
   // filled by the launcher
-  int Fc, n_chunks, n_parts, S_t, pow2;
+  int lgFc, n_chunks, n_parts, S_t, pow2, x_vec4;
 };
 
 struct BwdArgs {
@@ -61,7 +59,7 @@ struct BwdArgs {
   int F, B, D;
   int epi, relu;
   // filled by the launcher
-  int Fc, Wf, n_chunks, n_parts, S_t, pow2;
+  int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4;
 };
 
 // error plumbing (ple_capi.cu)
@@ -74,7 +72,7 @@ size_t device_max_smem_optin();
 
 int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cudaStream_t st);
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
-int backward_vec(int64_t D);
+int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
 
 }  // namespace ple

@@ -1,0 +1,92 @@
+// ple_simd.cuh - packed fp32x2 arithmetic, packed low-precision conversions
+// and cp.async helpers for sm_100a (inline PTX).
+//
+// fma/add.rn.f32x2 (PTX ISA 8.6, sm_100+) process two fp32 lanes per
+// instruction with the same rounding as two scalar fmaf/__fadd_rn calls, so
+// results are bit-identical to the scalar formulation.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace ple {
+
+typedef unsigned long long f2_t;  // two packed fp32 values (lo = first element)
+
+__device__ __forceinline__ f2_t pack2(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(f2_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
+  f2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2_t add2(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2_t mul2(f2_t a, f2_t b) {
+  f2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// max(v, 0) propagating NaN (torch.relu semantics).
+__device__ __forceinline__ float relu_nan(float v) {
+  float d;
+  asm("max.NaN.f32 %0, %1, 0f00000000;" : "=f"(d) : "f"(v));
+  return d;
+}
+
+// Packed round-to-nearest-even conversion of (lo, hi) to a 16-bit pair.
+template <typename T> __device__ __forceinline__ unsigned cvt_pack(float lo, float hi);
+template <> __device__ __forceinline__ unsigned cvt_pack<__nv_bfloat16>(float lo, float hi) {
+  unsigned d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+template <> __device__ __forceinline__ unsigned cvt_pack<__half>(float lo, float hi) {
+  unsigned d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// Widen a 16-bit pair back to fp32.
+template <typename T> __device__ __forceinline__ void widen_pack(unsigned p, float& lo, float& hi);
+template <> __device__ __forceinline__ void widen_pack<__nv_bfloat16>(unsigned p, float& lo, float& hi) {
+  lo = __uint_as_float(p << 16);
+  hi = __uint_as_float(p & 0xffff0000u);
+}
+template <> __device__ __forceinline__ void widen_pack<__half>(unsigned p, float& lo, float& hi) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&p);
+  const float2 f = __half22float2(h);
+  lo = f.x;
+  hi = f.y;
+}
+
+// Round two fp32 values through T (identity for float).
+template <typename T>
+__device__ __forceinline__ void round2(float& lo, float& hi) {
+  if constexpr (!std::is_same<T, float>::value) widen_pack<T>(cvt_pack<T>(lo, hi), lo, hi);
+}
+
+// ---------------------------------------------------------------- cp.async
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+}  // namespace ple
