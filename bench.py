@@ -88,6 +88,15 @@ class ClockSampler:
                  "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # wait for nvidia-smi's first sample so that the timed region is covered from its start
+        self.n_pre = 0
+        deadline = time.time() + 5.0
+        while self.proc is not None and time.time() < deadline:
+            lines = Path(self.path).read_text().splitlines()
+            if lines:
+                self.n_pre = len(lines)
+                break
+            time.sleep(0.01)
         self.t0 = time.time()
 
     def stop(self) -> dict:
@@ -104,6 +113,9 @@ class ClockSampler:
             if len(parts) >= 9:
                 rows.append(parts)
         os.unlink(self.path)
+        # samples taken after the timed region began; the last pre-start sample if the region was shorter
+        # than the sampling period
+        rows = rows[self.n_pre:] or rows[-1:]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -220,12 +232,14 @@ def main() -> int:
     def fwd():
         _native.check(lib.ple_embeddings_forward(
             x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(), W.data_ptr(), P(bias), P(w0),
-            P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, code[o_dtype], y.data_ptr(), sp), "forward")
+            P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, code[o_dtype], y.data_ptr(), 3, None,
+            sp), "forward")
 
     def bwd():
         _native.check(lib.ple_embeddings_backward(
             g.data_ptr(), code[o_dtype], x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(),
-            W.data_ptr(), P(bias), P(w0), P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, gx.data_ptr(),
+            W.data_ptr(), P(bias), P(w0), P(b0), epi, int(relu), code[q_dtype], n_local, F, B, D, None, 3,
+            gx.data_ptr(),
             gW.data_ptr(), P(gb), P(gw0), P(gb0), wsp.data_ptr(), ws_bytes, sp), "backward")
 
     def allreduce():

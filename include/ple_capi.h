@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 1
+#define PLE_ABI_VERSION 2
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -104,8 +104,9 @@ size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t ma
  *     r_k <g, q(W[phys k])> + [k > 0 and x == e_k] r_{k-1} <g, q(W[k-1])>
  *   grad_weight[F, B, D] (may be NULL; padding rows are written as zero):
  *     grad_W[i, phys(j)] = sum_{k_b = j} q(t_b) g_b + sum_{k_b > j} g_b
- *   bin_indices is accepted for interface parity and may be NULL; bins are
- *   recomputed from x.  The result is bitwise deterministic.
+ *   bin_indices (optional, may be NULL) are the forward's bins; when NULL they
+ *   are recomputed from x.  Values are clamped to [0, n_i - 1].  The result is
+ *   bitwise deterministic.
  */
 int ple_backward(const void* grad_output, int grad_dtype, const float* x,
                  const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
@@ -119,20 +120,24 @@ int ple_backward(const void* grad_output, int grad_dtype, const float* x,
  *   epilogue A: y = act(x_ple + bias); epilogue B: y = (x * w0 + b0) + act(x_ple)
  *   act = ReLU when activation != 0.  x_ple is computed as in ple_forward with
  *   rounding through compute_dtype (F32 = plain fp32; BF16 / F16 = autocast);
- *   the epilogue runs in fp32 and the result is stored as output_dtype.
+ *   the epilogue runs in fp32 and the result is stored as output_dtype.  With
+ *   epilogue B and a 16-bit output_dtype, x_ple is rounded once, at the store.
+ *   bin_indices[N, F] (optional, may be NULL) receives the bins as in
+ *   ple_forward, for reuse by the backward.
  */
 int ple_embeddings_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
                            const int32_t* n_bins, const float* weight, const float* bias,
                            const float* w0, const float* b0, int epilogue, int activation,
                            int compute_dtype, int64_t batch, int64_t n_features,
                            int64_t max_n_bins, int64_t d_embedding, int output_dtype,
-                           void* output, void* stream);
+                           void* output, int bin_index_dtype, void* bin_indices, void* stream);
 
 /*
  * Fused embeddings backward: every gradient of ple_embeddings_forward from the
  * upstream gradient in one pass over grad_output.  Gradient pointers may be
  * NULL when not needed; grad_bias is used with epilogue A, grad_w0 / grad_b0
- * with epilogue B.  Parameter gradients are written (not accumulated) and are
+ * with epilogue B.  bin_indices (optional) are the forward's bins, as in
+ * ple_backward.  Parameter gradients are written (not accumulated) and are
  * bitwise deterministic.
  */
 int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float* x,
@@ -140,10 +145,10 @@ int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float
                             const int32_t* n_bins, const float* weight, const float* bias,
                             const float* w0, const float* b0, int epilogue, int activation,
                             int compute_dtype, int64_t batch, int64_t n_features,
-                            int64_t max_n_bins, int64_t d_embedding, float* grad_x,
-                            float* grad_weight, float* grad_bias, float* grad_w0,
-                            float* grad_b0, void* workspace, size_t workspace_bytes,
-                            void* stream);
+                            int64_t max_n_bins, int64_t d_embedding, const void* bin_indices,
+                            int bin_index_dtype, float* grad_x, float* grad_weight,
+                            float* grad_bias, float* grad_w0, float* grad_b0, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

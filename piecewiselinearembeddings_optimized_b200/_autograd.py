@@ -4,8 +4,9 @@
 the inputs and the bin indices, marks ``bin_indices`` non-differentiable,
 does not materialise missing gradients, and calls ``backward`` only for the
 gradients that are needed.  ``embeddings_forward`` (the fused module path)
-calls ``embeddings_backward``, which returns every gradient of the fused
-forward (x, weight, bias or linear0) in one pass over ``grad_output``.
+calls ``embeddings_backward``, which finds the bins again and returns every
+gradient of the fused forward (x, weight, bias or linear0) in one pass over
+``grad_output``.
 Double backward is not implemented.
 """
 from __future__ import annotations
@@ -68,7 +69,7 @@ def _embeddings_backward(ctx: Any, grad_output):
     if g.dtype != ctx.compute_dtype and g.dtype != torch.float32:
         g = g.float()
     gx, gw, gb, gw0, gb0 = torch.ops.rtdl_num_embeddings_cuda.embeddings_backward(
-        g, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, ctx.epilogue, ctx.activation,
+        g, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, None, ctx.epilogue, ctx.activation,
         ctx.compute_dtype, bool(need[0]), bool(need[4]), bool(need[5]), bool(need[6] or need[7]),
     )
     return (

@@ -85,7 +85,7 @@ def _embeddings_forward_fake(x, bin_edges, inv_bin_widths, n_bins, weight, bias,
 
 @torch.library.register_fake("rtdl_num_embeddings_cuda::embeddings_backward")
 def _embeddings_backward_fake(grad_output, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0,
-                              epilogue: int, activation: bool, compute_dtype: torch.dtype,
+                              bin_indices, epilogue: int, activation: bool, compute_dtype: torch.dtype,
                               compute_grad_x: bool, compute_grad_weight: bool, compute_grad_bias: bool,
                               compute_grad_linear0: bool):
     torch._check(grad_output.ndim == 3, lambda: "grad_output must have shape [N, F, D]")

@@ -66,10 +66,10 @@ def capi() -> ctypes.CDLL:
     lib.ple_backward.restype = I
     lib.ple_backward.argtypes = [P, I, P, P, P, P, P, P, I, I64, I64, I64, I64, P, P, P, SZ, P]
     lib.ple_embeddings_forward.restype = I
-    lib.ple_embeddings_forward.argtypes = [P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64, I, P, P]
+    lib.ple_embeddings_forward.argtypes = [P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64, I, P, I, P, P]
     lib.ple_embeddings_backward.restype = I
     lib.ple_embeddings_backward.argtypes = [P, I, P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64,
-                                            P, P, P, P, P, P, SZ, P]
+                                            P, I, P, P, P, P, P, P, SZ, P]
     _capi = lib
     return lib
 

@@ -176,12 +176,14 @@ at::Tensor ple_embeddings_forward_op(const at::Tensor& x, const at::Tensor& bin_
   const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
   at::Tensor out = at::empty({N, F, D}, weight.options().dtype(output_dtype));
   if (out.numel() == 0) return out;
+  // bin indices are not requested: the fused backward finds the bins itself, which costs less than
+  // writing and re-reading a byte per (sample, feature)
   check_status(ple_embeddings_forward(x.data_ptr<float>(), bin_edges.data_ptr<float>(),
                                       inv_bin_widths.data_ptr<float>(), n_bins.data_ptr<int32_t>(),
                                       weight.data_ptr<float>(), ptr_or_null(bias), ptr_or_null(w0),
                                       ptr_or_null(b0), (int)epilogue, activation ? 1 : 0,
                                       to_code(compute_dtype), N, F, B, D, to_code(output_dtype), out.data_ptr(),
-                                      stream_of(x)),
+                                      PLE_DTYPE_U8, nullptr, stream_of(x)),
                "rtdl_num_embeddings_cuda::embeddings_forward");
   return out;
 }
@@ -190,8 +192,9 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
     const at::Tensor& grad_output, const at::Tensor& x, const at::Tensor& bin_edges,
     const at::Tensor& inv_bin_widths, const at::Tensor& n_bins, const at::Tensor& weight,
     const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& w0,
-    const std::optional<at::Tensor>& b0, int64_t epilogue, bool activation, at::ScalarType compute_dtype,
-    bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, bool compute_grad_linear0) {
+    const std::optional<at::Tensor>& b0, const std::optional<at::Tensor>& bin_indices, int64_t epilogue,
+    bool activation, at::ScalarType compute_dtype, bool compute_grad_x, bool compute_grad_weight,
+    bool compute_grad_bias, bool compute_grad_linear0) {
   check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
   check_param(bias, weight, "bias");
   check_param(w0, weight, "w0");
@@ -205,6 +208,13 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
               "grad_output shape must be [N, F, D]");
   TORCH_CHECK(to_code(grad_output.scalar_type()) >= 0 && to_code(grad_output.scalar_type()) <= PLE_DTYPE_BF16,
               "grad_output must be float32, float16, or bfloat16");
+  if (bin_indices.has_value()) {
+    TORCH_CHECK(bin_indices->is_cuda() && bin_indices->device() == x.device(), "bin_indices must be on x's device");
+    TORCH_CHECK(bin_indices->is_contiguous(), "bin_indices must be contiguous");
+    TORCH_CHECK(bin_indices->scalar_type() == bin_index_dtype(B), "bin_indices has an invalid dtype");
+    TORCH_CHECK(bin_indices->dim() == 2 && bin_indices->size(0) == N && bin_indices->size(1) == F,
+                "bin_indices shape must be [N, F]");
+  }
   c10::cuda::CUDAGuard guard(x.device());
   auto opt = weight.options();
   const bool want_bias = compute_grad_bias && epilogue == PLE_EPILOGUE_A;
@@ -221,6 +231,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
                    bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(), n_bins.data_ptr<int32_t>(),
                    weight.data_ptr<float>(), ptr_or_null(bias), ptr_or_null(w0), ptr_or_null(b0), (int)epilogue,
                    activation ? 1 : 0, to_code(compute_dtype), N, F, B, D,
+                   bin_indices.has_value() ? bin_indices->data_ptr() : nullptr,
+                   bin_indices.has_value() ? to_code(bin_indices->scalar_type()) : PLE_DTYPE_U8,
                    compute_grad_x ? gx.data_ptr<float>() : nullptr,
                    compute_grad_weight ? gw.data_ptr<float>() : nullptr, want_bias ? gb.data_ptr<float>() : nullptr,
                    want_l0 ? gw0.data_ptr<float>() : nullptr, want_l0 ? gb0.data_ptr<float>() : nullptr,
@@ -245,8 +257,8 @@ TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
       "ScalarType output_dtype) -> Tensor");
   m.def(
       "embeddings_backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, "
-      "Tensor n_bins, Tensor weight, Tensor? bias, Tensor? w0, Tensor? b0, int epilogue, bool activation, "
-      "ScalarType compute_dtype, bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, "
+      "Tensor n_bins, Tensor weight, Tensor? bias, Tensor? w0, Tensor? b0, Tensor? bin_indices, "
+      "int epilogue, bool activation, ScalarType compute_dtype, bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, "
       "bool compute_grad_linear0) -> (Tensor grad_x, Tensor grad_weight, Tensor grad_bias, Tensor grad_w0, "
       "Tensor grad_b0)");
 }

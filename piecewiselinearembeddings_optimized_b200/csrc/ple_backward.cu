@@ -15,8 +15,9 @@
 // one or a few (chunk, sample range) segments.  16 warps = Fc features x Wf
 // warps.  Per segment the chunk's tables are staged and H/U zeroed; per tile
 // of S_t samples (x arrives by cp.async one tile ahead):
-//   A  bin search of every pair, per-(feature, quarter, bin) counts (integer
-//      shared atomics: order independent);
+//   A  bin of every pair (the forward's bin indices when given, else a bin
+//      search), per-(feature, quarter, bin) counts (integer shared atomics:
+//      order independent);
 //   B  exclusive scan of the counts (bin-major, quarter-minor);
 //   C  stable counting sort: each warp ranks its quarter with __match_any_sync,
 //      so the sorted order is a pure function of the input;
@@ -26,9 +27,10 @@
 //      the active bin's T/S rows and running H/U sums in registers and
 //      flushing a run to the shared H/U histogram once, by its only owner (the
 //      segment in which it starts); a segment's first run goes to a carry
-//      slot.  grad_x is reduced across the row's lanes and scattered to a
-//      natural-order buffer;
-//   E  carries are added in segment order, grad_x rows stored coalesced.
+//      slot.  Each lane writes its share of grad_x to a per-(sample, lane)
+//      partial slot;
+//   E  carries are added in segment order; grad_x partials are summed and
+//      stored coalesced.
 // At the end of a segment a suffix scan over bins turns H/U into grad_W and
 // the partial goes to the workspace; ple_bwd_finalize_kernel sums the
 // partials of each feature in CTA order.  No floating-point atomics:
@@ -43,13 +45,14 @@ namespace ple {
 
 struct BwdLayout {
   float *sT, *sS, *sH, *sU, *sE, *sR, *sGX, *sCarry, *sXb;
-  int2* sEnt;
+  float2* sEnt;     // sorted (x, q(t))
+  unsigned* sMeta;  // sorted s | k << 16 | tie << 31
   uint8_t* sKey;
   int *sN, *sCnt, *sCarryBin;
 };
 
 struct BwdDims {
-  int Fc, Wf, S_t, G;
+  int Fc, Wf, S_t, G, nc;
 };
 
 __host__ __device__ __forceinline__ size_t bwd_layout_bytes(const BwdArgs& a, const BwdDims& m, BwdLayout* L,
@@ -63,8 +66,9 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(const BwdArgs& a, co
   };
   unsigned char* pT = take(4 * tab * 4);
   unsigned char* pCarry = take((size_t)m.Fc * m.G * 2 * a.D * 4);
-  unsigned char* pGX = take((size_t)m.Fc * m.S_t * 4);
+  unsigned char* pGX = take((size_t)m.Fc * m.S_t * m.nc * 4);  // grad_x partials [Fc][S_t][nc]
   unsigned char* pEnt = take((size_t)m.Fc * m.S_t * 8);
+  unsigned char* pMeta = take((size_t)m.Fc * m.S_t * 4);
   unsigned char* pXb = take((size_t)2 * m.S_t * m.Fc * 4);
   unsigned char* pE = take((size_t)a.pow2 * m.Fc * 4);
   unsigned char* pR = take((size_t)a.B * m.Fc * 4);
@@ -79,7 +83,8 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(const BwdArgs& a, co
     L->sU = L->sH + tab;
     L->sCarry = reinterpret_cast<float*>(pCarry);
     L->sGX = reinterpret_cast<float*>(pGX);
-    L->sEnt = reinterpret_cast<int2*>(pEnt);
+    L->sEnt = reinterpret_cast<float2*>(pEnt);
+    L->sMeta = reinterpret_cast<unsigned*>(pMeta);
     L->sXb = reinterpret_cast<float*>(pXb);
     L->sE = reinterpret_cast<float*>(pE);
     L->sR = reinterpret_cast<float*>(pR);
@@ -109,17 +114,6 @@ __device__ __forceinline__ void warp_exclusive_scan(int* cnt, int m, int lane) {
     cnt[j] = run;
     run += c;
   }
-}
-
-// Sum over the nc lanes of a row group (lanes r*nc .. r*nc+nc-1); result in c == 0.
-__device__ __forceinline__ float row_reduce(float v, int c, int nc) {
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    if (off >= nc) break;
-    const float o = __shfl_down_sync(0xffffffffu, v, off);
-    if (c + off < nc) v += o;
-  }
-  return v;
 }
 
 // Raw gradient chunk of VEC elements of GT (kept packed until use).
@@ -173,7 +167,231 @@ template <typename QT> __device__ __forceinline__ float zero_round_threshold() {
   else return 2.98023223876953125e-08f;                                                           // 2^-25
 }
 
-constexpr int kWalkUnroll = 4;
+// gradient rows gathered ahead per lane group: 4 for chunks up to 16 bytes, 2 for 32-byte chunks
+template <typename GT, int VEC> constexpr int walk_unroll() { return sizeof(GT) * VEC >= 32 ? 2 : (sizeof(GT) * VEC >= 16 && VEC >= 8 ? 2 : 4); }
+
+// VEC fp32 values of one D-row chunk held as packed pairs (VEC >= 2) or a
+// scalar (VEC == 1), so the walk's arithmetic maps onto fp32x2 instructions.
+template <int VEC> struct Row {
+  static constexpr int NP = VEC >= 2 ? VEC / 2 : 1;
+  f2_t p[NP];  // VEC == 1 uses the low half of p[0]
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int e = 0; e < NP; ++e) p[e] = 0ull;
+  }
+  __device__ __forceinline__ void lds(const float* src) {
+    if constexpr (VEC >= 4) {
+#pragma unroll
+      for (int e = 0; e < NP; e += 2) {
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(src + 2 * e);
+        p[e] = v.x;
+        p[e + 1] = v.y;
+      }
+    } else if constexpr (VEC == 2) {
+      p[0] = *reinterpret_cast<const unsigned long long*>(src);
+    } else {
+      p[0] = (f2_t)__float_as_uint(*src);
+    }
+  }
+  __device__ __forceinline__ void ldg(const float* src) {
+    if constexpr (VEC >= 4) {
+#pragma unroll
+      for (int e = 0; e < NP; e += 2) {
+        const ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2*>(src + 2 * e));
+        p[e] = v.x;
+        p[e + 1] = v.y;
+      }
+    } else if constexpr (VEC == 2) {
+      p[0] = __ldg(reinterpret_cast<const unsigned long long*>(src));
+    } else {
+      p[0] = (f2_t)__float_as_uint(__ldg(src));
+    }
+  }
+  __device__ __forceinline__ void sts(float* dst) const {
+    if constexpr (VEC >= 4) {
+#pragma unroll
+      for (int e = 0; e < NP; e += 2)
+        *reinterpret_cast<ulonglong2*>(dst + 2 * e) = make_ulonglong2(p[e], p[e + 1]);
+    } else if constexpr (VEC == 2) {
+      *reinterpret_cast<unsigned long long*>(dst) = p[0];
+    } else {
+      *dst = __uint_as_float((unsigned)p[0]);
+    }
+  }
+  __device__ __forceinline__ float lo(int e) const {
+    float a, b;
+    unpack2(p[e], a, b);
+    return a;
+  }
+};
+
+// Add a run's sums into the shared histogram (H, U) or, for the first run of
+// the segment (which may have started in the previous segment), into the
+// segment's carry slot.
+template <int VEC>
+__device__ __forceinline__ void flush_run(const Row<VEC>& H, const Row<VEC>& U, bool& first_run, int k_cur,
+                                          float* carry, int* carry_bin, int D, int c, float* h, float* u) {
+  if (first_run) {
+    H.sts(carry);
+    U.sts(carry + D);
+    if (c == 0) *carry_bin = k_cur;
+    first_run = false;
+  } else {
+    Row<VEC> hv, uv;
+    hv.lds(h);
+    uv.lds(u);
+#pragma unroll
+    for (int e = 0; e < Row<VEC>::NP; ++e) {
+      hv.p[e] = add2(hv.p[e], H.p[e]);
+      uv.p[e] = add2(uv.p[e], U.p[e]);
+    }
+    hv.sts(h);
+    uv.sts(u);
+  }
+}
+
+// One lane group's walk over its segment of a feature's bin-sorted samples.
+template <typename QT, typename GT, int VEC, int EPI, bool RELU>
+__device__ __forceinline__ void walk_segment(
+    const BwdLayout& L, const float2* ents, const unsigned* metas, int my_len, int trips, const GT* grow,
+    int64_t gstride, int my_i, int lgFc, int D, int cd, int c, int nc, float* carry, int* carry_bin, float* gx_row,
+    bool do_gx, const Row<VEC>& pw0, const Row<VEC>& pbias, Row<VEC>& acc_w0, Row<VEC>& acc_b0) {
+  constexpr int NP = Row<VEC>::NP;
+  int k_cur = -1;
+  bool first_run = true;
+  float r_k = 0.f, r_km1 = 0.f;
+  Row<VEC> Tk, Sk, Skm1, Hrun, Urun;
+  Tk.zero(); Sk.zero(); Skm1.zero(); Hrun.zero(); Urun.zero();
+  const float thr = zero_round_threshold<QT>();
+  const int kstride = D << lgFc;
+  float* hbase = L.sH + my_i * D + cd;
+  float* ubase = L.sU + my_i * D + cd;
+
+  constexpr int kWalkUnroll = walk_unroll<GT, VEC>();
+  for (int base = 0; base < trips; base += kWalkUnroll) {
+    float2 ent[kWalkUnroll];
+    unsigned meta[kWalkUnroll];
+    GRaw<GT, VEC> graw[kWalkUnroll];
+#pragma unroll
+    for (int u = 0; u < kWalkUnroll; ++u) {
+      const int step = base + u;
+      meta[u] = 0xffffu << 16;  // bin sentinel for lanes past their segment
+      if (step < my_len) {
+        ent[u] = ents[step];
+        meta[u] = metas[step];
+        ldg_raw<GT, VEC>(graw[u], grow + (int64_t)(meta[u] & 0xffffu) * gstride);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kWalkUnroll; ++u) {
+      const bool live = base + u < my_len;
+      const int k = (meta[u] >> 16) & 0x7fff;
+      if (live && k != k_cur) {
+        if (k_cur >= 0)
+          flush_run<VEC>(Hrun, Urun, first_run, k_cur, carry, carry_bin, D, c, hbase + k_cur * kstride,
+                         ubase + k_cur * kstride);
+        k_cur = k;
+        const int to = (k << lgFc) * D + my_i * D + cd;
+        Tk.lds(L.sT + to);
+        Sk.lds(L.sS + to);
+        r_k = L.sR[(k << lgFc) + my_i];
+        Hrun.zero();
+        Urun.zero();
+      }
+      const bool tie = live && (meta[u] >> 31);
+      float gx = 0.f;
+      if (live) {
+        const float xv = ent[u].x, tq = ent[u].y;
+        if constexpr (VEC >= 2) {
+          const f2_t t2 = pack2(tq, tq), x2 = pack2(xv, xv);
+          f2_t d2 = 0ull, dw2 = 0ull;
+          f2_t q[NP];
+#pragma unroll
+          for (int e = 0; e < NP; ++e) {
+            float g0, g1;
+            raw_pair<GT, VEC>(graw[u], 2 * e, g0, g1);
+            float q0 = g0, q1 = g1;
+            if constexpr (RELU) {
+              float p0, p1;
+              unpack2(fma2(t2, Sk.p[e], Tk.p[e]), p0, p1);
+              if constexpr (EPI == kEpiA) {
+                round2<QT>(p0, p1);
+                float b0, b1;
+                unpack2(pbias.p[e], b0, b1);
+                p0 += b0;
+                p1 += b1;
+                q0 = p0 > 0.f ? g0 : 0.f;
+                q1 = p1 > 0.f ? g1 : 0.f;
+              } else {
+                q0 = p0 > thr ? g0 : 0.f;
+                q1 = p1 > thr ? g1 : 0.f;
+              }
+            }
+            if constexpr (!std::is_same<GT, QT>::value && !std::is_same<QT, float>::value) round2<QT>(q0, q1);
+            q[e] = pack2(q0, q1);
+            Hrun.p[e] = add2(Hrun.p[e], q[e]);
+            Urun.p[e] = fma2(t2, q[e], Urun.p[e]);
+            d2 = fma2(q[e], Sk.p[e], d2);
+            if constexpr (EPI == kEpiB) {
+              const f2_t gg = pack2(g0, g1);
+              acc_w0.p[e] = fma2(gg, x2, acc_w0.p[e]);
+              acc_b0.p[e] = add2(acc_b0.p[e], gg);
+              dw2 = fma2(gg, pw0.p[e], dw2);
+            }
+          }
+          float lo, hi;
+          unpack2(d2, lo, hi);
+          gx = r_k * (lo + hi);
+          if constexpr (EPI == kEpiB) {
+            unpack2(dw2, lo, hi);
+            gx += lo + hi;
+          }
+          if (__any_sync(__activemask(), tie)) {  // edge sub-gradient (x == e_k), rare for continuous x
+            const int km1 = k_cur > 0 ? k_cur - 1 : 0;
+            Skm1.lds(L.sS + (km1 << lgFc) * D + my_i * D + cd);
+            r_km1 = L.sR[(km1 << lgFc) + my_i];
+            f2_t dp2 = 0ull;
+#pragma unroll
+            for (int e = 0; e < NP; ++e) dp2 = fma2(q[e], Skm1.p[e], dp2);
+            unpack2(dp2, lo, hi);
+            if (tie) gx += r_km1 * (lo + hi);
+          }
+        } else {
+          const float g0 = raw_one<GT, VEC>(graw[u]);
+          float q0 = g0;
+          const float s0 = Sk.lo(0), t0v = Tk.lo(0);
+          if constexpr (RELU) {
+            float p0 = fmaf(tq, s0, t0v);
+            if constexpr (EPI == kEpiA) {
+              p0 = quantize<QT>(p0) + pbias.lo(0);
+              q0 = p0 > 0.f ? g0 : 0.f;
+            } else {
+              q0 = p0 > thr ? g0 : 0.f;
+            }
+          }
+          if constexpr (!std::is_same<GT, QT>::value) q0 = quantize<QT>(q0);
+          Hrun.p[0] = (f2_t)__float_as_uint(Hrun.lo(0) + q0);
+          Urun.p[0] = (f2_t)__float_as_uint(fmaf(tq, q0, Urun.lo(0)));
+          gx = r_k * (q0 * s0);
+          if (tie) {
+            const int km1 = k_cur - 1;
+            gx += L.sR[(km1 << lgFc) + my_i] * (q0 * L.sS[(km1 << lgFc) * D + my_i * D + cd]);
+          }
+          if constexpr (EPI == kEpiB) {
+            acc_w0.p[0] = (f2_t)__float_as_uint(fmaf(g0, xv, acc_w0.lo(0)));
+            acc_b0.p[0] = (f2_t)__float_as_uint(acc_b0.lo(0) + g0);
+            gx += g0 * pw0.lo(0);
+          }
+        }
+      }
+      if (do_gx && live) gx_row[(meta[u] & 0xffffu) * nc] = gx;  // this lane's partial of the row
+    }
+  }
+  if (my_len > 0 && k_cur >= 0)
+    flush_run<VEC>(Hrun, Urun, first_run, k_cur, carry, carry_bin, D, c, hbase + k_cur * kstride,
+                   ubase + k_cur * kstride);
+}
+
 
 template <typename QT, typename GT, int VEC, int EPI, bool RELU>
 __global__ void __launch_bounds__(kBwdThreads, 1)
@@ -186,7 +404,7 @@ ple_bwd_kernel(const BwdArgs a) {
   const int Rint = 32 / nc;
   const int G = Wf * Rint;
   BwdLayout L;
-  bwd_layout_bytes(a, BwdDims{Fc, Wf, S_t, G}, &L, smem_raw);
+  bwd_layout_bytes(a, BwdDims{Fc, Wf, S_t, G, nc}, &L, smem_raw);
 
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int lane = tid & 31, wid = tid >> 5;
@@ -277,18 +495,15 @@ ple_bwd_kernel(const BwdArgs a) {
     }
 
     // per-lane epilogue parameters and linear0 accumulators (packed pairs)
-    constexpr int NP = VEC / 2 > 0 ? VEC / 2 : 1;
-    FV<VEC> pw0, pbias;
-    f2_t acc_w0[NP], acc_b0[NP];
-    float acc_w0_1 = 0.f, acc_b0_1 = 0.f;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) { pw0.v[e] = 0.f; pbias.v[e] = 0.f; }
-#pragma unroll
-    for (int e = 0; e < NP; ++e) { acc_w0[e] = pack2(0.f, 0.f); acc_b0[e] = pack2(0.f, 0.f); }
+    Row<VEC> pw0, pbias, acc_w0, acc_b0;
+    pw0.zero();
+    pbias.zero();
+    acc_w0.zero();
+    acc_b0.zero();
     if (grp_live) {
       const int64_t po = (int64_t)(f0 + my_i) * D + cd;
-      if constexpr (EPI == kEpiA && RELU) pbias = ldg_f32vec<float, VEC>(a.bias + po);
-      if constexpr (EPI == kEpiB) pw0 = ldg_f32vec<float, VEC>(a.w0 + po);
+      if constexpr (EPI == kEpiA && RELU) pbias.ldg(a.bias + po);
+      if constexpr (EPI == kEpiB) pw0.ldg(a.w0 + po);
     }
 
     int buf = 0;
@@ -299,25 +514,20 @@ ple_bwd_kernel(const BwdArgs a) {
       cp_async_wait_all();
       __syncthreads();  // x tile landed, counts zeroed, previous tile finished
       if (t0 + S_t < s_end) load_x(t0 + S_t, (int)min64(S_t, s_end - t0 - S_t), L.sXb + (buf ^ 1) * S_t * Fc);
-      // prefetch the next tile's gradient rows of this chunk into L2
-      if (t0 + S_t < s_end) {
-        const int64_t nt0 = t0 + S_t;
-        const int nns = (int)min64(S_t, s_end - nt0);
-        const int row_bytes = fc * D * (int)sizeof(GT);
-        const int lines = row_bytes / 128 + 2;
-        for (int q = tid; q < nns * lines; q += nthr) {
-          const int s = q / lines, l = q - s * lines;
-          const uintptr_t rp = reinterpret_cast<uintptr_t>(gptr + ((nt0 + s) * a.F + f0) * D);
-          const uintptr_t pp = (rp & ~(uintptr_t)127) + (uintptr_t)l * 128;
-          if (pp < rp + row_bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
-        }
-      }
       // ---- A: bins and counts
       for (int p = tid; p < (ns << lgFc); p += nthr) {
         const int s = p >> lgFc, i = p & (Fc - 1);
         if (i < fc) {
-          const float xv = sX[p];
-          const int k = logical_bin(edge_count(xv, L.sE, Fc, i, pow2), L.sN[i]);
+          int k;
+          if (a.bin_idx != nullptr) {
+            const int64_t pair = (t0 + s) * a.F + f0 + i;
+            k = a.bin_idx_bytes == 1 ? (int)reinterpret_cast<const uint8_t*>(a.bin_idx)[pair]
+              : a.bin_idx_bytes == 2 ? (int)reinterpret_cast<const int16_t*>(a.bin_idx)[pair]
+                                     : reinterpret_cast<const int32_t*>(a.bin_idx)[pair];
+            k = k < 0 ? 0 : (k >= L.sN[i] ? L.sN[i] - 1 : k);
+          } else {
+            k = logical_bin(edge_count(sX[p], L.sE, Fc, i, pow2), L.sN[i]);
+          }
           L.sKey[(i << lgSt) + s] = (uint8_t)k;
           atomicAdd(&L.sCnt[((i * B + k) << lgWf) + (s >> lg_q)], 1);
         }
@@ -344,7 +554,12 @@ ple_bwd_kernel(const BwdArgs a) {
             pos0 = __shfl_sync(peers, pos0, leader);
             if (lane == leader) *cur = pos0 + __popc(peers);
             const float xv = sX[(s << lgFc) + my_i];
-            L.sEnt[(my_i << lgSt) + pos0 + rank] = make_int2(__float_as_int(xv), s | (k << 16));
+            const float e_k = L.sE[(k << lgFc) + my_i];
+            const float t = (xv - e_k) * L.sR[(k << lgFc) + my_i];
+            const unsigned tie = (k > 0 && xv == e_k) ? 0x80000000u : 0u;
+            const int pos = (my_i << lgSt) + pos0 + rank;
+            L.sEnt[pos] = make_float2(xv, quantize<QT>(t));
+            L.sMeta[pos] = (unsigned)s | ((unsigned)k << 16) | tie;
           }
           __syncwarp();
         }
@@ -358,153 +573,13 @@ ple_bwd_kernel(const BwdArgs a) {
         int trips = my_len;
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) trips = max(trips, __shfl_xor_sync(0xffffffffu, trips, off));
-        int k_cur = -1;
-        bool first_run = true;
-        float e_k = 0.f, r_k = 0.f, r_km1 = 0.f;
-        FV<VEC> Tk, Sk, Skm1, Hrun, Urun;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) { Tk.v[e] = Sk.v[e] = Skm1.v[e] = Hrun.v[e] = Urun.v[e] = 0.f; }
         float* carry = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
         if (grp_live && c == 0) L.sCarryBin[my_i * G + g_seg] = -1;
-        const int2* ents = L.sEnt + (my_i << lgSt) + seg_lo;
-        const GT* grow = gptr + (t0 * a.F + f0 + my_i) * (int64_t)D + cd;
-        const int64_t gstride = (int64_t)a.F * D;
-
-        auto flush = [&]() {
-          if (first_run) {
-            sts<VEC>(carry, Hrun);
-            sts<VEC>(carry + D, Urun);
-            if (c == 0) L.sCarryBin[my_i * G + g_seg] = k_cur;
-            first_run = false;
-          } else {
-            float* h = L.sH + ((k_cur << lgFc) + my_i) * D + cd;
-            float* u = L.sU + ((k_cur << lgFc) + my_i) * D + cd;
-            FV<VEC> hv = lds<VEC>(h), uv = lds<VEC>(u);
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) { hv.v[e] += Hrun.v[e]; uv.v[e] += Urun.v[e]; }
-            sts<VEC>(h, hv);
-            sts<VEC>(u, uv);
-          }
-        };
-
-        for (int base = 0; base < trips; base += kWalkUnroll) {
-          int2 ent[kWalkUnroll];
-          GRaw<GT, VEC> graw[kWalkUnroll];
-#pragma unroll
-          for (int u = 0; u < kWalkUnroll; ++u) {
-            const int step = base + u;
-            ent[u] = make_int2(0, -1);
-#pragma unroll
-            for (int w = 0; w < GRaw<GT, VEC>::kWords; ++w) graw[u].w[w] = 0u;
-            if (step < my_len) {
-              ent[u] = ents[step];
-              ldg_raw<GT, VEC>(graw[u], grow + (int64_t)(ent[u].y & 0xffff) * gstride);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kWalkUnroll; ++u) {
-            const bool live = base + u < my_len;
-            const int k = ent[u].y >> 16;
-            if (live && k != k_cur) {
-              if (k_cur >= 0) flush();
-              k_cur = k;
-              const int to = ((k << lgFc) + my_i) * D + cd;
-              Tk = lds<VEC>(L.sT + to);
-              Sk = lds<VEC>(L.sS + to);
-              e_k = L.sE[(k << lgFc) + my_i];
-              r_k = L.sR[(k << lgFc) + my_i];
-              if (k > 0) {
-                Skm1 = lds<VEC>(L.sS + to - (D << lgFc));
-                r_km1 = L.sR[((k - 1) << lgFc) + my_i];
-              }
-#pragma unroll
-              for (int e = 0; e < VEC; ++e) { Hrun.v[e] = 0.f; Urun.v[e] = 0.f; }
-            }
-            float gx = 0.f;
-            if (live) {
-              const float xv = __int_as_float(ent[u].x);
-              const float t = (xv - e_k) * r_k;
-              const float tq = quantize<QT>(t);
-              const bool edge_tie = (k > 0) && (xv == e_k);
-              float dot = 0.f, dot_prev = 0.f, dot_w0 = 0.f;
-              if constexpr (VEC >= 2) {
-                const f2_t t2 = pack2(tq, tq);
-                const f2_t x2 = pack2(xv, xv);
-                f2_t d2 = pack2(0.f, 0.f), dp2 = pack2(0.f, 0.f), dw2 = pack2(0.f, 0.f);
-#pragma unroll
-                for (int e = 0; e < VEC; e += 2) {
-                  float g0, g1;
-                  raw_pair<GT, VEC>(graw[u], e, g0, g1);
-                  float q0 = g0, q1 = g1;
-                  if constexpr (RELU) {
-                    float p0, p1;
-                    unpack2(fma2(t2, pack2(Sk.v[e], Sk.v[e + 1]), pack2(Tk.v[e], Tk.v[e + 1])), p0, p1);
-                    if constexpr (EPI == kEpiA) {
-                      round2<QT>(p0, p1);
-                      p0 += pbias.v[e];
-                      p1 += pbias.v[e + 1];
-                      q0 = p0 > 0.f ? g0 : 0.f;
-                      q1 = p1 > 0.f ? g1 : 0.f;
-                    } else {
-                      const float thr = zero_round_threshold<QT>();
-                      q0 = p0 > thr ? g0 : 0.f;
-                      q1 = p1 > thr ? g1 : 0.f;
-                    }
-                  }
-                  if constexpr (!std::is_same<GT, QT>::value && !std::is_same<QT, float>::value) round2<QT>(q0, q1);
-                  const f2_t q2 = pack2(q0, q1);
-                  const f2_t h2 = add2(pack2(Hrun.v[e], Hrun.v[e + 1]), q2);
-                  const f2_t u2 = fma2(t2, q2, pack2(Urun.v[e], Urun.v[e + 1]));
-                  unpack2(h2, Hrun.v[e], Hrun.v[e + 1]);
-                  unpack2(u2, Urun.v[e], Urun.v[e + 1]);
-                  d2 = fma2(q2, pack2(Sk.v[e], Sk.v[e + 1]), d2);
-                  dp2 = fma2(q2, pack2(Skm1.v[e], Skm1.v[e + 1]), dp2);
-                  if constexpr (EPI == kEpiB) {
-                    const f2_t gg = pack2(g0, g1);
-                    acc_w0[e >> 1] = fma2(gg, x2, acc_w0[e >> 1]);
-                    acc_b0[e >> 1] = add2(acc_b0[e >> 1], gg);
-                    dw2 = fma2(gg, pack2(pw0.v[e], pw0.v[e + 1]), dw2);
-                  }
-                }
-                float lo, hi;
-                unpack2(d2, lo, hi);
-                dot = lo + hi;
-                unpack2(dp2, lo, hi);
-                dot_prev = lo + hi;
-                unpack2(dw2, lo, hi);
-                dot_w0 = lo + hi;
-              } else {
-                const float g0 = raw_one<GT, VEC>(graw[u]);
-                float q0 = g0;
-                if constexpr (RELU) {
-                  float p0 = fmaf(tq, Sk.v[0], Tk.v[0]);
-                  if constexpr (EPI == kEpiA) {
-                    p0 = quantize<QT>(p0) + pbias.v[0];
-                    q0 = p0 > 0.f ? g0 : 0.f;
-                  } else {
-                    q0 = p0 > zero_round_threshold<QT>() ? g0 : 0.f;
-                  }
-                }
-                if constexpr (!std::is_same<GT, QT>::value) q0 = quantize<QT>(q0);
-                Hrun.v[0] += q0;
-                Urun.v[0] = fmaf(tq, q0, Urun.v[0]);
-                dot = q0 * Sk.v[0];
-                dot_prev = q0 * Skm1.v[0];
-                if constexpr (EPI == kEpiB) {
-                  acc_w0_1 = fmaf(g0, xv, acc_w0_1);
-                  acc_b0_1 += g0;
-                  dot_w0 = g0 * pw0.v[0];
-                }
-              }
-              gx = r_k * dot + (edge_tie ? r_km1 * dot_prev : 0.f) + dot_w0;
-            }
-            if (do_gx) {
-              gx = row_reduce(gx, c, nc);
-              if (live && c == 0) L.sGX[(my_i << lgSt) + (ent[u].y & 0xffff)] = gx;
-            }
-          }
-        }
-        if (grp_live && k_cur >= 0) flush();
+        walk_segment<QT, GT, VEC, EPI, RELU>(
+            L, L.sEnt + (my_i << lgSt) + seg_lo, L.sMeta + (my_i << lgSt) + seg_lo, my_len, trips,
+            gptr + (t0 * a.F + f0 + my_i) * (int64_t)D + cd, (int64_t)a.F * D, my_i, lgFc, D, cd, c, nc,
+            carry, L.sCarryBin + my_i * G + g_seg, L.sGX + (my_i << lgSt) * nc + c, do_gx, pw0, pbias, acc_w0,
+            acc_b0);
       }
       __syncthreads();
       // ---- E: carries in segment order; grad_x rows
@@ -522,7 +597,12 @@ ple_bwd_kernel(const BwdArgs a) {
       if (do_gx) {
         for (int p = tid; p < (ns << lgFc); p += nthr) {
           const int s = p >> lgFc, i = p & (Fc - 1);
-          if (i < fc) a.grad_x[(t0 + s) * a.F + f0 + i] = L.sGX[(i << lgSt) + s];
+          if (i < fc) {
+            const float* part = L.sGX + ((i << lgSt) + s) * nc;
+            float v = 0.f;
+            for (int cc = 0; cc < nc; ++cc) v += part[cc];
+            a.grad_x[(t0 + s) * a.F + f0 + i] = v;
+          }
         }
       }
     }
@@ -533,16 +613,8 @@ ple_bwd_kernel(const BwdArgs a) {
     if constexpr (EPI == kEpiB) {
       if (grp_live) {
         float* cp = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
-        if constexpr (VEC >= 2) {
-#pragma unroll
-          for (int e = 0; e < VEC; e += 2) {
-            unpack2(acc_w0[e >> 1], cp[e], cp[e + 1]);
-            unpack2(acc_b0[e >> 1], cp[D + e], cp[D + e + 1]);
-          }
-        } else {
-          cp[0] = acc_w0_1;
-          cp[D] = acc_b0_1;
-        }
+        acc_w0.sts(cp);
+        acc_b0.sts(cp + D);
       }
       __syncthreads();
       for (int colx = tid; colx < fc * D; colx += nthr) {
@@ -637,7 +709,7 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
     const int lgWf = 4 - lgFc;  // 16 warps
     const int G = (1 << lgWf) * (32 / nc);
     for (int lgSt = 10; lgSt >= 7; --lgSt) {
-      BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G};
+      BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G, nc};
       const size_t bytes = bwd_layout_bytes(a, m, nullptr, nullptr);
       if (bytes <= optin) {
         a.lgFc = lgFc;

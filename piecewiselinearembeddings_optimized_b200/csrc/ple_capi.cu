@@ -163,10 +163,10 @@ int ple_embeddings_forward(const float* x, const float* bin_edges, const float* 
                            const int32_t* n_bins, const float* weight, const float* bias, const float* w0,
                            const float* b0, int epilogue, int activation, int compute_dtype, int64_t batch,
                            int64_t n_features, int64_t max_n_bins, int64_t d_embedding, int output_dtype,
-                           void* output, void* stream) {
+                           void* output, int bin_index_dtype, void* bin_indices, void* stream) {
   return forward_impl(x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, epilogue, activation,
                       compute_dtype, batch, n_features, max_n_bins, d_embedding, output_dtype, output,
-                      PLE_DTYPE_U8, nullptr, stream);
+                      bin_index_dtype, bin_indices, stream);
 }
 
 size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t max_n_bins,
@@ -179,8 +179,9 @@ size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t ma
 static int backward_impl(const void* g, int grad_dtype, const float* x, const float* edges, const float* inv_w,
                          const int32_t* n_bins, const float* W, const float* bias, const float* w0,
                          const float* b0, int epi, int relu, int compute_dtype, int64_t N, int64_t F,
-                         int64_t B, int64_t D, float* grad_x, float* grad_W, float* grad_bias,
-                         float* grad_w0, float* grad_b0, void* ws, size_t ws_bytes, void* stream) {
+                         int64_t B, int64_t D, const void* bin_idx, int bin_idx_dtype, float* grad_x,
+                         float* grad_W, float* grad_bias, float* grad_w0, float* grad_b0, void* ws,
+                         size_t ws_bytes, void* stream) {
   g_msg[0] = 0;
   int st = check_sizes(N, F, B, D);
   if (st) return st;
@@ -213,7 +214,18 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
   if (!aligned(g, (size_t)vec * dtype_size(grad_dtype)) || !aligned(w0, (size_t)vec * 4) ||
       !aligned(bias, (size_t)vec * 4))
     return set_error(PLE_ERR_ALIGNMENT, "grad_output / bias / w0 must be aligned to the vector width");
+  int idx_bytes = 0;
+  if (bin_idx) {
+    switch (bin_idx_dtype) {
+      case PLE_DTYPE_U8: idx_bytes = 1; break;
+      case PLE_DTYPE_I16: idx_bytes = 2; break;
+      case PLE_DTYPE_I32: idx_bytes = 4; break;
+      default: return set_error(PLE_ERR_INVALID_ARGUMENT, "bin index dtype must be U8, I16 or I32");
+    }
+  }
   BwdArgs a{};
+  a.bin_idx = bin_idx;
+  a.bin_idx_bytes = idx_bytes;
   a.g = g; a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.W = W;
   a.bias = bias; a.w0 = w0; a.b0 = b0;
   a.grad_x = grad_x; a.grad_W = grad_W; a.grad_bias = grad_bias; a.grad_w0 = grad_w0; a.grad_b0 = grad_b0;
@@ -227,23 +239,23 @@ int ple_backward(const void* grad_output, int grad_dtype, const float* x, const 
                  const void* bin_indices, int bin_index_dtype, int64_t batch, int64_t n_features,
                  int64_t max_n_bins, int64_t d_embedding, float* grad_x, float* grad_weight, void* workspace,
                  size_t workspace_bytes, void* stream) {
-  (void)bin_indices;
-  (void)bin_index_dtype;
   return backward_impl(grad_output, grad_dtype, x, bin_edges, inv_bin_widths, n_bins, weight, nullptr, nullptr,
-                       nullptr, kEpiNone, 0, grad_dtype, batch, n_features, max_n_bins, d_embedding, grad_x,
-                       grad_weight, nullptr, nullptr, nullptr, workspace, workspace_bytes, stream);
+                       nullptr, kEpiNone, 0, grad_dtype, batch, n_features, max_n_bins, d_embedding, bin_indices,
+                       bin_index_dtype, grad_x, grad_weight, nullptr, nullptr, nullptr, workspace, workspace_bytes,
+                       stream);
 }
 
 int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float* x, const float* bin_edges,
                             const float* inv_bin_widths, const int32_t* n_bins, const float* weight,
                             const float* bias, const float* w0, const float* b0, int epilogue, int activation,
                             int compute_dtype, int64_t batch, int64_t n_features, int64_t max_n_bins,
-                            int64_t d_embedding, float* grad_x, float* grad_weight, float* grad_bias,
-                            float* grad_w0, float* grad_b0, void* workspace, size_t workspace_bytes,
-                            void* stream) {
+                            int64_t d_embedding, const void* bin_indices, int bin_index_dtype, float* grad_x,
+                            float* grad_weight, float* grad_bias, float* grad_w0, float* grad_b0, void* workspace,
+                            size_t workspace_bytes, void* stream) {
   return backward_impl(grad_output, grad_dtype, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0,
-                       epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, grad_x,
-                       grad_weight, grad_bias, grad_w0, grad_b0, workspace, workspace_bytes, stream);
+                       epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, bin_indices,
+                       bin_index_dtype, grad_x, grad_weight, grad_bias, grad_w0, grad_b0, workspace,
+                       workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -15,9 +15,9 @@ enum { kEpiNone = PLE_EPILOGUE_NONE, kEpiA = PLE_EPILOGUE_A, kEpiB = PLE_EPILOGU
 constexpr int kBwdThreads = 512;
 
 // forward tuning
-constexpr int kFwdMaxThreads = 256;
+constexpr int kFwdMaxThreads = 512;
 constexpr size_t kFwdTableBudget = 64 * 1024;
-constexpr int kFwdPairsPerTile = 2048;
+constexpr int kFwdPairsPerTile = 1024;
 
 struct FwdArgs {
   const float* x;
@@ -35,11 +35,13 @@ struct FwdArgs {
   int F, B, D;
   int epi, relu;
   // filled by the launcher
-  int lgFc, n_chunks, n_parts, S_t, pow2, x_vec4;
+  int lgFc, n_chunks, S_t, pow2, ldE, x_vec4;
 };
 
 struct BwdArgs {
   const void* g;
+  const void* bin_idx;  // optional forward bins (U8 / I16 / I32)
+  int bin_idx_bytes;
   const float* x;
   const float* edges;
   const float* inv_w;

@@ -64,10 +64,10 @@ def test_forward_rejects_missing_tables_and_bad_dtypes():
     assert lib.ple_forward(FAKE, FAKE, FAKE, FAKE, FAKE, 4, 3, 4, 8, 7, FAKE, 3, None, None) == 1
     assert lib.ple_forward(FAKE, FAKE, FAKE, FAKE, FAKE, 4, 3, 4, 8, 0, FAKE, 0, FAKE, None) == 1
     st = lib.ple_embeddings_forward(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 1, 0, 0,
-                                    4, 3, 4, 8, 0, FAKE, None)
+                                    4, 3, 4, 8, 0, FAKE, 3, None, None)
     assert st == 1 and b"bias" in lib.ple_last_error_message()
     st = lib.ple_embeddings_forward(FAKE, FAKE, FAKE, FAKE, FAKE, None, FAKE, None, 2, 0, 0,
-                                    4, 3, 4, 8, 0, FAKE, None)
+                                    4, 3, 4, 8, 0, FAKE, 3, None, None)
     assert st == 1 and b"w0" in lib.ple_last_error_message()
 
 
@@ -120,13 +120,12 @@ def test_direct_capi_forward_backward_match_oracle(cuda_device):
     gb0 = torch.empty(f, d, device=cuda_device)
     _native.check(lib.ple_embeddings_backward(
         tg.data_ptr(), 0, tx.data_ptr(), te.data_ptr(), tr.data_ptr(), tn.data_ptr(), tw.data_ptr(), None,
-        tw0.data_ptr(), tb0.data_ptr(), 2, 1, 0, 256, f, b, d, gx.data_ptr(), gw.data_ptr(), None,
-        gw0.data_ptr(), gb0.data_ptr(), ws.data_ptr(), ws_bytes, stream), "ple_embeddings_backward")
+        tw0.data_ptr(), tb0.data_ptr(), 2, 1, 0, 256, f, b, d, idx.data_ptr(), 3, gx.data_ptr(), gw.data_ptr(),
+        None, gw0.data_ptr(), gb0.data_ptr(), ws.data_ptr(), ws_bytes, stream), "ple_embeddings_backward")
     ref = o.embeddings_backward(g, x, edges, inv_w, nb, w, version="B", activation=True, w0=w0, b0=b0)
     np.testing.assert_allclose(gx.cpu().numpy(), ref["grad_x"], rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(gw.cpu().numpy(), ref["grad_W"], rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(gw0.cpu().numpy(), ref["grad_w0"], rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(gb0.cpu().numpy(), ref["grad_b0"], rtol=1e-4, atol=1e-5)
+    for got, key in ((gw, "grad_W"), (gw0, "grad_w0"), (gb0, "grad_b0")):
+        o.assert_reduction_close(got.cpu().numpy(), ref[key], ref["abs"][key], err_msg=key)
 
 
 @pytest.mark.gpu

@@ -94,7 +94,7 @@ def test_fake_tensor_shapes():
         assert y.shape == (5, 4, 8) and y.dtype == torch.bfloat16 and idx.dtype == torch.uint8
         y2 = ops.embeddings_forward(x, e, r, n, w, None, None, None, 0, False, torch.float32, torch.float32)
         assert y2.shape == (5, 4, 8)
-        gx, gw, gb, gw0, gb0 = ops.embeddings_backward(y2, x, e, r, n, w, None, None, None, 0, False,
+        gx, gw, gb, gw0, gb0 = ops.embeddings_backward(y2, x, e, r, n, w, None, None, None, None, 0, False,
                                                        torch.float32, True, True, True, True)
         assert gx.shape == (5, 4) and gw.shape == (4, 5, 8) and gb.numel() == 0
 

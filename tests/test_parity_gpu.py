@@ -40,15 +40,19 @@ def to_dev(dev, *arrays):
     return [None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in arrays]
 
 
-def run_fused(ops, dev, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, mode, out_mode=None):
+def run_fused(ops, dev, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, mode, out_mode=None,
+              reuse_bins=False):
     out_mode = out_mode or "f32"
     tx, te, tr, tn, tw, tb, tw0, tb0 = to_dev(dev, x, edges, inv_w, nb, w, bias, w0, b0)
     y = ops.embeddings_forward(tx, te, tr, tn, tw, tb, tw0, tb0, EPI[version], relu, TORCH_DT[mode],
                                TORCH_DT[out_mode])
     res = {"y": y.float().cpu().numpy()}
     if g is not None:
+        # the bin indices of the x_ple op (reference contract) are also accepted by the fused backward
+        idx = ops.forward(tx, te, tr, tn, tw, torch.float32)[1] if reuse_bins else None
         tg = torch.from_numpy(g).to(dev).to(TORCH_DT[out_mode])
-        gx, gw, gb, gw0, gb0 = ops.embeddings_backward(tg, tx, te, tr, tn, tw, tb, tw0, tb0, EPI[version], relu,
+        gx, gw, gb, gw0, gb0 = ops.embeddings_backward(tg, tx, te, tr, tn, tw, tb, tw0, tb0,
+                                                       idx, EPI[version], relu,
                                                        TORCH_DT[mode], True, True, True, True)
         res.update(grad_x=gx.cpu().numpy(), grad_W=gw.cpu().numpy())
         if version == "A":
@@ -91,7 +95,8 @@ def test_fused_fp32_matches_oracle(ops, cuda_device, case, version, relu, d):
     edges, inv_w, nb = o.pad_bins(bins)
     w, bias, w0, b0 = cases.init_params(len(bins), edges.shape[1] - 1, d, version, d)
     g = np.random.default_rng(3000 + d).standard_normal((128, len(bins), d)).astype(np.float32)
-    res = run_fused(ops, cuda_device, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, "f32")
+    res = run_fused(ops, cuda_device, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, "f32",
+                    reuse_bins=(d % 2 == 0))
     compare_fused(res, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, "f32")
 
 
@@ -259,6 +264,7 @@ def test_full_size_properties(ops, cuda_device, name):
     od = TORCH_DT[wl.out_mode]
     y = ops.embeddings_forward(tx, te, tr, tn, tw, tb, tw0, tb0, EPI[wl.version], wl.activation,
                                TORCH_DT[wl.mode], od)
+    idx = ops.forward(tx, te, tr, tn, tw, torch.float32)[1]
     rows = np.random.default_rng(0).choice(wl.n, 256, replace=False)
     rows.sort()
     y_ref, _, _ = o.embeddings_forward(wl.x[rows], edges, inv_w, nb, wl.weight, version=wl.version,
@@ -269,7 +275,7 @@ def test_full_size_properties(ops, cuda_device, name):
                                **(LOW_TOL if low else FWD_TOL))
     del y
     tg = torch.from_numpy(g).to(dev).to(od)
-    full = ops.embeddings_backward(tg, tx, te, tr, tn, tw, tb, tw0, tb0, EPI[wl.version], wl.activation,
+    full = ops.embeddings_backward(tg, tx, te, tr, tn, tw, tb, tw0, tb0, idx, EPI[wl.version], wl.activation,
                                    TORCH_DT[wl.mode], True, True, True, True)
     ref_rows = o.embeddings_backward(g[rows], wl.x[rows], edges, inv_w, nb, wl.weight, version=wl.version,
                                      activation=wl.activation, bias=wl.bias, w0=wl.w0, b0=wl.b0, mode=wl.mode)
@@ -277,9 +283,10 @@ def test_full_size_properties(ops, cuda_device, name):
                                **(LOW_GRAD_TOL if low else GRAD_TOL))
     shards = torch.tensor_split(torch.arange(wl.n, device=dev), 4)
     acc = [torch.zeros_like(t) for t in full[1:]]
-    for idx in shards:
-        part = ops.embeddings_backward(tg[idx].contiguous(), tx[idx].contiguous(), te, tr, tn, tw, tb, tw0, tb0,
-                                       EPI[wl.version], wl.activation, TORCH_DT[wl.mode], False, True, True, True)
+    for sel in shards:
+        part = ops.embeddings_backward(tg[sel].contiguous(), tx[sel].contiguous(), te, tr, tn, tw, tb, tw0, tb0,
+                                       None, EPI[wl.version], wl.activation, TORCH_DT[wl.mode], False, True, True,
+                                       True)
         for a_, p_ in zip(acc, part[1:]):
             if p_.numel():
                 a_ += p_
