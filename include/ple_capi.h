@@ -150,6 +150,46 @@ int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float
                             float* grad_bias, float* grad_w0, float* grad_b0, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/*
+ * ple_embeddings_backward_noalloc: ple_embeddings_backward with its workspace
+ * taken from scratch memory built into the library instead of from the caller.
+ * No counterpart in the reference (its backward allocates through torch).
+ *
+ * For callers that cannot hand over device memory of their own: a host binding
+ * over plain C FFI (Go, Java, a ctypes script) that holds only its input and
+ * output buffers and has no device allocator to draw a workspace from, and a
+ * serving process that reserves its whole memory budget at start-up and may
+ * not allocate afterwards.  This entry point itself allocates nothing on any
+ * call: the scratch is a static device array of PLE_NOALLOC_SCRATCH_BYTES
+ * (16 MiB) per device, placed when the library's module is loaded.
+ *
+ *   - Same arguments, results and status codes as ple_embeddings_backward,
+ *     without workspace / workspace_bytes.
+ *   - Sizes whose workspace (ple_backward_workspace_size) exceeds
+ *     PLE_NOALLOC_SCRATCH_BYTES are rejected with PLE_ERR_WORKSPACE before
+ *     anything is launched; use ple_embeddings_backward for those.
+ *   - The scratch does not need to start at zero: every slot that the
+ *     finalize step reads is written earlier in the same call.
+ *   - The first call on each device looks up the scratch address
+ *     (cudaGetSymbolAddress, once per device); make that first call before
+ *     any stream capture on the device.
+ *   - One scratch per device, shared by all calls: two calls whose kernels
+ *     can overlap on the same device (different streams, or host threads
+ *     without ordering) race on it and corrupt each other's results.  Order
+ *     such calls on one stream.
+ */
+#define PLE_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, const float* x,
+                                    const float* bin_edges, const float* inv_bin_widths,
+                                    const int32_t* n_bins, const float* weight, const float* bias,
+                                    const float* w0, const float* b0, int epilogue, int activation,
+                                    int compute_dtype, int64_t batch, int64_t n_features,
+                                    int64_t max_n_bins, int64_t d_embedding,
+                                    const void* bin_indices, int bin_index_dtype, float* grad_x,
+                                    float* grad_weight, float* grad_bias, float* grad_w0,
+                                    float* grad_b0, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

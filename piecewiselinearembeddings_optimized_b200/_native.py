@@ -70,6 +70,9 @@ def capi() -> ctypes.CDLL:
     lib.ple_embeddings_backward.restype = I
     lib.ple_embeddings_backward.argtypes = [P, I, P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64,
                                             P, I, P, P, P, P, P, P, SZ, P]
+    lib.ple_embeddings_backward_noalloc.restype = I
+    lib.ple_embeddings_backward_noalloc.argtypes = [P, I, P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64,
+                                                    P, I, P, P, P, P, P, P]
     _capi = lib
     return lib
 

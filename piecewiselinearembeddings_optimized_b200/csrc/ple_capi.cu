@@ -93,6 +93,36 @@ int pick_vec(int64_t D, int max_vec, std::initializer_list<std::pair<const void*
 int device_sm_count() { return props().sms; }
 size_t device_max_smem_optin() { return props().smem_optin; }
 
+// ---------------------------------------------------------------- no-allocation backward
+// The scratch lives in this module's static device memory; its address is
+// looked up once per device and cached.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PLE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+struct ScratchSlot {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+ScratchSlot g_scratch[kMaxDevices];
+}  // namespace
+
+static int noalloc_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return set_error(PLE_ERR_UNSUPPORTED, "device ordinal above 63");
+  ScratchSlot& slot = g_scratch[dev];
+  std::call_once(slot.once, [&slot] {
+    slot.err = cudaGetSymbolAddress(&slot.ptr, g_noalloc_scratch);
+  });
+  if (slot.err != cudaSuccess || slot.ptr == nullptr)
+    return set_cuda_error(slot.err != cudaSuccess ? slot.err : cudaErrorInvalidSymbol,
+                          "cudaGetSymbolAddress(no-allocation scratch)");
+  *ptr = slot.ptr;
+  return PLE_OK;
+}
+
 }  // namespace ple
 
 using namespace ple;
@@ -256,6 +286,34 @@ int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float
                        epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, bin_indices,
                        bin_index_dtype, grad_x, grad_weight, grad_bias, grad_w0, grad_b0, workspace,
                        workspace_bytes, stream);
+}
+
+int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, const float* x,
+                                    const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
+                                    const float* weight, const float* bias, const float* w0, const float* b0,
+                                    int epilogue, int activation, int compute_dtype, int64_t batch,
+                                    int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                                    const void* bin_indices, int bin_index_dtype, float* grad_x,
+                                    float* grad_weight, float* grad_bias, float* grad_w0, float* grad_b0,
+                                    void* stream) {
+  g_msg[0] = 0;
+  int st = check_sizes(batch, n_features, max_n_bins, d_embedding);
+  if (st) return st;
+  const size_t need = backward_workspace_bytes(batch < 1 ? 1 : batch, n_features, max_n_bins, d_embedding);
+  if (need > PLE_NOALLOC_SCRATCH_BYTES) {
+    snprintf(g_msg, sizeof(g_msg),
+             "ple_embeddings_backward_noalloc: this shape needs %zu bytes of workspace, more than the %zu-byte "
+             "built-in scratch; call ple_embeddings_backward with a workspace of ple_backward_workspace_size() "
+             "bytes",
+             need, (size_t)PLE_NOALLOC_SCRATCH_BYTES);
+    return PLE_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch))) return st;
+  return backward_impl(grad_output, grad_dtype, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0,
+                       epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, bin_indices,
+                       bin_index_dtype, grad_x, grad_weight, grad_bias, grad_w0, grad_b0, scratch,
+                       (size_t)PLE_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 }  // extern "C"
