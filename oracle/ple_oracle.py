@@ -282,8 +282,8 @@ def embeddings_backward(g, x, edges, inv_w, n_bins, W, *, version="A", activatio
                         bias=None, w0=None, b0=None, mode="f32"):
     """Autograd of ``embeddings_forward``.
 
-    ReLU passes the gradient where its input is ``> 0`` (torch
-    ``threshold_backward``). The x_ple branch receives ``q(g * mask)``: under
+    ReLU blocks the gradient where its input is ``<= 0`` and passes it
+    elsewhere, NaN inputs included (torch ``threshold_backward``). The x_ple branch receives ``q(g * mask)``: under
     autocast the gradient of the low-precision ``x_ple`` is cast to that type
     before the reference backward op (``_autograd.py:68-80``). The bias and
     linear0 gradients are fp32 reductions of the unrounded gradient.
@@ -295,7 +295,7 @@ def embeddings_backward(g, x, edges, inv_w, n_bins, W, *, version="A", activatio
     _, z, _ = embeddings_forward(x, edges, inv_w, n_bins, W, version=version,
                                  activation=activation, bias=bias, w0=w0, b0=b0,
                                  mode=mode)
-    g_ple = g * (z > 0) if activation else g
+    g_ple = np.where(z <= 0, np.float32(0.0), g) if activation else g
     g_ple = g_ple.astype(np.float32)
     grad_x, grad_W, abs_W = x_ple_backward(quantize(g_ple, mode), x, edges, inv_w, n_bins, W, mode,
                                            with_abs=True)

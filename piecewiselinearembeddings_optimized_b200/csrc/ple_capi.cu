@@ -241,8 +241,11 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
   if (!aligned(ws, 16)) return set_error(PLE_ERR_WORKSPACE, "workspace must be 16-byte aligned");
   const int vec = backward_vec(D, dtype_size(grad_dtype));
   if (D / vec > 32) return set_error(PLE_ERR_UNSUPPORTED, "backward: odd d_embedding above 32 is not supported");
-  if (!aligned(g, (size_t)vec * dtype_size(grad_dtype)) || !aligned(w0, (size_t)vec * 4) ||
-      !aligned(bias, (size_t)vec * 4))
+  // widest power of two (<= 16 bytes) dividing a lane's chunk of grad_output / of an fp32 parameter row
+  const size_t chunk = (size_t)vec * dtype_size(grad_dtype);
+  const size_t g_align = chunk % 16 == 0 ? 16 : chunk % 8 == 0 ? 8 : chunk % 4 == 0 ? 4 : 2;
+  const size_t p_align = vec % 4 == 0 ? 16 : (size_t)vec * 4;
+  if (!aligned(g, g_align) || !aligned(w0, p_align) || !aligned(bias, p_align))
     return set_error(PLE_ERR_ALIGNMENT, "grad_output / bias / w0 must be aligned to the vector width");
   int idx_bytes = 0;
   if (bin_idx) {
