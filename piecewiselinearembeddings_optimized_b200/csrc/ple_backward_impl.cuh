@@ -56,6 +56,9 @@
 namespace ple {
 
 enum { kMaskNone = 0, kMaskRelu = 1, kMaskReluBias = 2 };
+// epilogue terms accumulated along the walk: none, sum g' (epilogue A bias), or linear0 (<g, w0>, sum g x,
+// sum g; epilogue B)
+enum { kEpvNone = 0, kEpvBias = 1, kEpvLin = 2 };
 
 struct BwdDims {
   int Fc, Wf, S_t, G, nc;  // G = lane groups per feature
@@ -78,7 +81,7 @@ struct BwdLayout {
   float *sCarry;             // [Fc][G][2][D]
   float2* sEnt;              // [Fc][S_t + G] sorted (q(t), meta bits: s | k << 16 | tie << 31), segment-major
   uint8_t* sKey;             // [Fc][S_t] bins of the tile
-  int *sN, *sCnt, *sCarryBin;
+  int *sN, *sCnt, *sCarryBin, *sTie;  // sTie[Fc]: the tile has an edge tie in feature i
 };
 
 __host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int pow2, const BwdDims& m,
@@ -100,6 +103,7 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int po
   unsigned char* pN = take((size_t)m.Fc * 4);
   unsigned char* pCnt = take((size_t)m.Fc * B * m.Wf * 4);
   unsigned char* pCB = take((size_t)m.Fc * m.G * 4);
+  unsigned char* pTie = take((size_t)m.Fc * 4);
   unsigned char* pKey = take((size_t)m.Fc * m.S_t);
   if (L) {
     L->sT = reinterpret_cast<float*>(pT);
@@ -115,6 +119,7 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int po
     L->sN = reinterpret_cast<int*>(pN);
     L->sCnt = reinterpret_cast<int*>(pCnt);
     L->sCarryBin = reinterpret_cast<int*>(pCB);
+    L->sTie = reinterpret_cast<int*>(pTie);
     L->sKey = reinterpret_cast<uint8_t*>(pKey);
   }
   return off;
@@ -293,13 +298,13 @@ template <typename GT, int VEC> struct WalkIn {
 
 template <typename GT, int VEC, int DEPTH>
 __device__ __forceinline__ void walk_fetch(WalkIn<GT, VEC> (&in)[DEPTH], const float2* ents, int estride, int base,
-                                           int len, const GT* grow, int64_t gstride) {
+                                           int len, const GT* grow, unsigned gstride) {
 #pragma unroll
   for (int u = 0; u < DEPTH; ++u) {
     const int step = base + u;
     if (step < len) {
       in[u].ent = ents[step * estride];
-      ldg_raw<GT, VEC>(in[u].g, grow + (int64_t)(__float_as_uint(in[u].ent.y) & 0xffffu) * gstride);
+      ldg_raw<GT, VEC>(in[u].g, grow + (unsigned long long)(__float_as_uint(in[u].ent.y) & 0xffffu) * gstride);
     }
   }
 }
@@ -317,13 +322,14 @@ struct WalkCtx {
   int kstride, lgFc, nc, D, c;
 };
 
-template <typename QT, typename GT, int VEC, int MASK, bool LIN, int DEPTH>
+template <typename QT, typename GT, int VEC, int MASK, int EPIV, int DEPTH>
 __device__ __forceinline__ void walk_block(const WalkCtx& w, WalkIn<GT, VEC> (&in)[DEPTH], int base, int len,
                                            int& k_cur, bool& first_run, float& r_k, Row<VEC>& Tk, Row<VEC>& Sk,
                                            Row<VEC>& Hrun, Row<VEC>& Urun, const Row<VEC>& pbias, Row<VEC>& braw,
-                                           const Row<VEC>& w0r, Row<VEC>& acc_w0, Row<VEC>& acc_b0, bool acc_bias,
+                                           const Row<VEC>& w0r, Row<VEC>& acc_w0, Row<VEC>& acc_b0, bool ties,
                                            bool do_gx) {
   constexpr int NP = Row<VEC>::NP;
+  constexpr bool LIN = EPIV == kEpvLin;
   const float thr = zero_round_threshold<QT>();
 #pragma unroll
   for (int u = 0; u < DEPTH; ++u) {
@@ -380,7 +386,7 @@ __device__ __forceinline__ void walk_block(const WalkCtx& w, WalkIn<GT, VEC> (&i
               q1 = p1 <= thr ? 0.f : g1;
             }
           }
-          if (acc_bias) braw.p[e] = add2(braw.p[e], pack2(q0, q1));
+          if constexpr (EPIV == kEpvBias) braw.p[e] = add2(braw.p[e], pack2(q0, q1));
           if constexpr (!std::is_same<GT, QT>::value && !std::is_same<QT, float>::value) round2<QT>(q0, q1);
           q[e] = pack2(q0, q1);
           Hrun.p[e] = add2(Hrun.p[e], q[e]);
@@ -412,7 +418,7 @@ __device__ __forceinline__ void walk_block(const WalkCtx& w, WalkIn<GT, VEC> (&i
             q0 = p0 <= thr ? 0.f : g0;
           }
         }
-        if (acc_bias) braw.p[0] = (f2_t)__float_as_uint(braw.lo(0) + q0);
+        if constexpr (EPIV == kEpvBias) braw.p[0] = (f2_t)__float_as_uint(braw.lo(0) + q0);
         if constexpr (!std::is_same<GT, QT>::value) q0 = quantize<QT>(q0);
         q[0] = (f2_t)__float_as_uint(q0);
         Hrun.p[0] = (f2_t)__float_as_uint(Hrun.lo(0) + q0);
@@ -420,7 +426,7 @@ __device__ __forceinline__ void walk_block(const WalkCtx& w, WalkIn<GT, VEC> (&i
         gx = r_k * (q0 * s0);
         if constexpr (LIN) gx += g0 * w0r.lo(0);
       }
-      if (__any_sync(__activemask(), tie)) {  // edge sub-gradient (x == e_k, k > 0): rare for continuous x
+      if (ties && __any_sync(__activemask(), tie)) {  // edge sub-gradient (x == e_k, k > 0): rare
         const int km1 = k_cur > 0 ? k_cur - 1 : 0;
         Row<VEC> Skm1;
         Skm1.lds(w.tS + km1 * w.kstride);
@@ -495,8 +501,9 @@ __device__ __forceinline__ void stage_tables(const BwdArgs& a, const BwdLayout& 
   }
 }
 
-template <typename QT, typename GT, int VEC, int MASK, bool LIN>
+template <typename QT, typename GT, int VEC, int MASK, int EPIV>
 __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a) {
+  constexpr bool LIN = EPIV == kEpvLin;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int DEPTH = walk_depth<GT, VEC>();
   const int lgFc = a.lgFc, lgWf = a.lgWf, lgSt = a.lgSt;
@@ -519,8 +526,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
   const int my_w = wid & (Wf - 1);
   const int g_seg = my_w * Rint + r;
   const bool do_gx = a.grad_x != nullptr;
-  // sum g' for epilogue A (bias); LIN kernels (epilogue B) accumulate sum g x / sum g instead
-  const bool acc_bias = !LIN && MASK != kMaskRelu && a.epi == kEpiA && a.grad_bias != nullptr;
+  constexpr bool acc_bias = EPIV == kEpvBias;  // sum g' for the epilogue-A bias gradient
   const GT* gptr = reinterpret_cast<const GT*>(a.g);
   const int lg_q = lgSt - lgWf;  // quarter length (log2)
 
@@ -659,6 +665,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
       // tile's carries were consumed before this tile's first barrier)
       for (int i = wid; i < fc; i += nthr >> 5) warp_exclusive_scan(L.sCnt + ((i * B) << lgWf), B << lgWf, lane);
       for (int idx = tid; idx < Fc * G; idx += nthr) L.sCarryBin[idx] = -1;
+      for (int idx = tid; idx < Fc; idx += nthr) L.sTie[idx] = 0;
       __syncthreads();
       // ---- C: stable scatter of each quarter into sorted order; sorted position p is stored at
       // (p % Lseg) * G + p / Lseg
@@ -687,6 +694,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
             const float e_k = L.sE[(k << lgFc) + my_i];
             const float t = (xv - e_k) * L.sR[(k << lgFc) + my_i];
             const unsigned tie = (k > 0 && xv == e_k) ? 0x80000000u : 0u;
+            if (tie) L.sTie[my_i] = 1;
             const unsigned pos = (unsigned)(pos0 + rank);
             const unsigned gq = pow2L ? pos >> lgL : __umulhi(pos, mL);
             L.sEnt[my_i * ES + (int)(pos - gq * (unsigned)Lseg) * G + (int)gq] =
@@ -724,7 +732,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
         w.c = c;
         const float2* ents = L.sEnt + my_i * ES + (g_seg < G ? g_seg : 0);
         const GT* grow = gptr + (t0 * a.F + f0 + my_i) * (int64_t)D + cd;
-        const int64_t gstride = (int64_t)a.F * D;
+        const unsigned gstride = (unsigned)a.F * (unsigned)D;
+        const bool ties = L.sTie[my_i] != 0;
         int k_cur = -1;
         bool first_run = true;
         float r_k = 0.f;
@@ -737,11 +746,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
         walk_fetch<GT, VEC, DEPTH>(ia, ents, G, 0, len, grow, gstride);
         for (int base = 0; base < trips; base += 2 * DEPTH) {
           walk_fetch<GT, VEC, DEPTH>(ib, ents, G, base + DEPTH, len, grow, gstride);
-          walk_block<QT, GT, VEC, MASK, LIN, DEPTH>(w, ia, base, len, k_cur, first_run, r_k, Tk, Sk, Hrun, Urun,
-                                                    pbias, braw, w0r, acc_w0, acc_b0, acc_bias, do_gx);
+          walk_block<QT, GT, VEC, MASK, EPIV, DEPTH>(w, ia, base, len, k_cur, first_run, r_k, Tk, Sk, Hrun, Urun,
+                                                     pbias, braw, w0r, acc_w0, acc_b0, ties, do_gx);
           walk_fetch<GT, VEC, DEPTH>(ia, ents, G, base + 2 * DEPTH, len, grow, gstride);
-          walk_block<QT, GT, VEC, MASK, LIN, DEPTH>(w, ib, base + DEPTH, len, k_cur, first_run, r_k, Tk, Sk, Hrun,
-                                                    Urun, pbias, braw, w0r, acc_w0, acc_b0, acc_bias, do_gx);
+          walk_block<QT, GT, VEC, MASK, EPIV, DEPTH>(w, ib, base + DEPTH, len, k_cur, first_run, r_k, Tk, Sk, Hrun,
+                                                     Urun, pbias, braw, w0r, acc_w0, acc_b0, ties, do_gx);
         }
         if (k_cur >= 0)
           flush_run<VEC>(Hrun, Urun, first_run, k_cur, w.carry, w.carry_bin, D, c, w.tH + k_cur * ts,
@@ -792,7 +801,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
     // ---- F: epilogue partials (fixed group order) and grad_W suffix scan
     __syncthreads();
     float* ws = a.ws + ((int64_t)blockIdx.x * a.max_segs + seg) * ((int64_t)Fc * (B + 3) * D);
-    if (LIN || acc_bias) {
+    if constexpr (LIN || acc_bias) {
       if (walk_live) {
         float* cp = L.sCarry + ((my_i * G + g_seg) * 2) * D + cd;
         acc_w0.sts(cp);  // sum g x, or sum g' (epilogue A)
@@ -836,13 +845,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
 int bwd_prepare(BwdArgs& a, int vec, size_t* smem, int* grid);
 int bwd_finalize(const BwdArgs& a, int grid, cudaStream_t st);
 
-template <typename QT, typename GT, int VEC, int MASK, bool LIN>
+template <typename QT, typename GT, int VEC, int MASK, int EPIV>
 int launch_bwd_t(BwdArgs a, cudaStream_t st) {
   size_t smem = 0;
   int grid = 0;
   const int prep = bwd_prepare(a, VEC, &smem, &grid);
   if (prep != PLE_OK) return prep;
-  auto kern = ple_bwd_kernel<QT, GT, VEC, MASK, LIN>;
+  auto kern = ple_bwd_kernel<QT, GT, VEC, MASK, EPIV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
   kern<<<grid, kBwdThreads, smem, st>>>(a);
@@ -851,15 +860,19 @@ int launch_bwd_t(BwdArgs a, cudaStream_t st) {
   return bwd_finalize(a, grid, st);
 }
 
-// Mask variant (ReLU with bias is epilogue A, plain ReLU is epilogue B) and whether the epilogue-B
-// terms are needed.
+// Mask variant (ReLU with bias is epilogue A, plain ReLU is epilogue B) and the epilogue terms the requested
+// gradients need.
 template <typename QT, typename GT, int VEC>
 int launch_bwd_mask(const BwdArgs& a, cudaStream_t st) {
   const bool lin = a.epi == kEpiB && (a.grad_x || a.grad_w0 || a.grad_b0);
-  if (a.relu && a.epi == kEpiA) return launch_bwd_t<QT, GT, VEC, kMaskReluBias, false>(a, st);
-  if (a.relu) return lin ? launch_bwd_t<QT, GT, VEC, kMaskRelu, true>(a, st)
-                         : launch_bwd_t<QT, GT, VEC, kMaskRelu, false>(a, st);
-  return lin ? launch_bwd_t<QT, GT, VEC, kMaskNone, true>(a, st) : launch_bwd_t<QT, GT, VEC, kMaskNone, false>(a, st);
+  const bool bias = a.epi == kEpiA && a.grad_bias;
+  if (a.relu && a.epi == kEpiA)
+    return bias ? launch_bwd_t<QT, GT, VEC, kMaskReluBias, kEpvBias>(a, st)
+                : launch_bwd_t<QT, GT, VEC, kMaskReluBias, kEpvNone>(a, st);
+  if (a.relu)
+    return lin ? launch_bwd_t<QT, GT, VEC, kMaskRelu, kEpvLin>(a, st) : launch_bwd_t<QT, GT, VEC, kMaskRelu, kEpvNone>(a, st);
+  if (lin) return launch_bwd_t<QT, GT, VEC, kMaskNone, kEpvLin>(a, st);
+  return bias ? launch_bwd_t<QT, GT, VEC, kMaskNone, kEpvBias>(a, st) : launch_bwd_t<QT, GT, VEC, kMaskNone, kEpvNone>(a, st);
 }
 
 template <typename QT, typename GT>
