@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 2
+#define PLE_ABI_VERSION 3
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -52,6 +52,12 @@ enum {
   PLE_EPILOGUE_NONE = 0, /* x_ple only (the reference op)                    */
   PLE_EPILOGUE_A = 1,    /* act(x_ple + bias)                                */
   PLE_EPILOGUE_B = 2     /* (x * w0 + b0) + act(x_ple)                       */
+};
+
+/* Layouts of the standalone encoding (ple_encoding_forward). */
+enum {
+  PLE_ENC_RAGGED = 0, /* [N, sum_i n_i]: feature-major, logical bin order, no padding       */
+  PLE_ENC_PADDED = 1  /* [N, F, B]: the weights' physical layout, zero padding columns   */
 };
 
 /* Status codes. */
@@ -189,6 +195,40 @@ int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, con
                                     const void* bin_indices, int bin_index_dtype, float* grad_x,
                                     float* grad_weight, float* grad_bias, float* grad_w0,
                                     float* grad_b0, void* stream);
+
+/*
+ * Standalone piecewise-linear encoding (upstream
+ * rtdl_num_embeddings.PiecewiseLinearEncoding; the reference has no CUDA path
+ * for it, only the x_ple op of which it is the inner factor).
+ *   column j of feature i (logical bin j < n_i):
+ *     t_j = (x - e_j) * r_j, clamped to <= 1 (j = 0), [0, 1] (middle bins),
+ *     >= 0 (j = n_i - 1); a single-bin feature is unclamped; NaN propagates.
+ *   layout PLE_ENC_RAGGED: output [N, total_cols], total_cols = sum_i n_i,
+ *     col_offsets[F + 1] (int64, device) = exclusive prefix of n_bins;
+ *   layout PLE_ENC_PADDED: output [N, F, B] (total_cols = F * B), the bins in
+ *     the weights' physical layout (last real bin at column B - 1), padding
+ *     columns 0; col_offsets may be NULL.
+ *   output_dtype F32 / F16 / BF16 (values computed in fp32, rounded once).
+ * Columns whose offsets disagree with n_bins are written as 0 (never read or
+ * written out of bounds).
+ */
+int ple_encoding_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                         const int32_t* n_bins, const int64_t* col_offsets, int layout,
+                         int64_t batch, int64_t n_features, int64_t max_n_bins, int64_t total_cols,
+                         int output_dtype, void* output, void* stream);
+
+/*
+ * Gradient of ple_encoding_forward with respect to x:
+ *   grad_x[b, i] = sum_j g[b, col(i, j)] * r_j * [lo_j <= t_j <= hi_j]
+ * (the clamp passes the gradient at its bounds, as torch.clamp's backward;
+ * no gradient where t_j is NaN).  grad_output has the forward's layout, in
+ * grad_dtype F32 / F16 / BF16; grad_x[N, F] fp32.
+ */
+int ple_encoding_backward(const void* grad_output, int grad_dtype, const float* x,
+                          const float* bin_edges, const float* inv_bin_widths,
+                          const int32_t* n_bins, const int64_t* col_offsets, int layout,
+                          int64_t batch, int64_t n_features, int64_t max_n_bins,
+                          int64_t total_cols, float* grad_x, void* stream);
 
 #ifdef __cplusplus
 }

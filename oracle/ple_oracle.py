@@ -380,3 +380,69 @@ def dense_forward(x, edges, inv_w, n_bins, W, *, version="A", activation=False,
     if version == "B":
         y = y + np.asarray(x, np.float64)[..., None] * w0[None] + b0[None]
     return y
+
+
+# ---------------------------------------------------------------- standalone encoding
+
+def _encoding_bounds(j, nb):
+    """Clamp bounds of logical column j of an nb-bin feature (upstream
+    ``PiecewiseLinearEncoding``'s column clamps; the position formula is the
+    reference's, backward_cuda.cu:194-196)."""
+    if nb == 1:
+        return -np.inf, np.inf
+    if j == 0:
+        return -np.inf, 1.0
+    if j == nb - 1:
+        return 0.0, np.inf
+    return 0.0, 1.0
+
+
+def encoding(x, edges, inv_w, n_bins, *, padded=False, dtype=np.float32):
+    """Materialised encoding: ``[N, sum n_i]`` (feature-major, logical bin
+    order) or, with ``padded``, ``[N, F, B]`` in the weights' physical layout.
+    ``dtype=np.float32`` evaluates ``(x - e_j) * r_j`` in fp32 (the kernel's
+    arithmetic); ``np.float64`` in double precision.  NaN propagates through
+    the clamps."""
+    x = np.asarray(x, dtype=dtype)
+    n, f = x.shape
+    b_max = edges.shape[1] - 1
+    cols = []
+    out = np.zeros((n, f, b_max), dtype=dtype) if padded else None
+    for i in range(f):
+        nb = int(n_bins[i])
+        for j in range(nb):
+            v = (x[:, i] - dtype(edges[i, j])) * dtype(inv_w[i, j])
+            lo, hi = _encoding_bounds(j, nb)
+            v = np.where(v < lo, dtype(lo), v)
+            v = np.where(v > hi, dtype(hi), v)
+            if padded:
+                out[:, i, b_max - 1 if j == nb - 1 else j] = v
+            else:
+                cols.append(v)
+    return out if padded else np.stack(cols, axis=1).astype(dtype)
+
+
+def encoding_grad_x(g, x, edges, inv_w, n_bins, *, padded=False):
+    """``grad_x[b, i] = sum_j g[b, col(i, j)] * r_j * [lo_j <= t_j <= hi_j]``
+    with t_j in fp32 (the kernel's mask) and the sum in float64; returns
+    ``(grad_x, sum of |terms|)``."""
+    x32 = np.asarray(x, dtype=np.float32)
+    n, f = x32.shape
+    b_max = edges.shape[1] - 1
+    g = np.asarray(g, dtype=np.float64)
+    gx = np.zeros((n, f))
+    ab = np.zeros((n, f))
+    c = 0
+    for i in range(f):
+        nb = int(n_bins[i])
+        for j in range(nb):
+            r = np.float32(inv_w[i, j])
+            t = (x32[:, i] - np.float32(edges[i, j])) * r
+            lo, hi = _encoding_bounds(j, nb)
+            m = (t >= lo) & (t <= hi)
+            col = g[:, i, b_max - 1 if j == nb - 1 else j] if padded else g[:, c + j]
+            term = np.where(m, col * np.float64(r), 0.0)
+            gx[:, i] += term
+            ab[:, i] += np.abs(term)
+        c += nb
+    return gx, ab

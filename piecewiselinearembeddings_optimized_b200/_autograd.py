@@ -86,3 +86,28 @@ torch.library.register_autograd(
     "rtdl_num_embeddings_cuda::embeddings_forward", _embeddings_backward,
     setup_context=_setup_embeddings_context,
 )
+
+# ---------------------------------------------------------------- standalone encoding
+
+
+def _setup_encoding_context(ctx: Any, inputs, output) -> None:
+    x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout, total_bins, _output_dtype = inputs
+    ctx.save_for_backward(x, bin_edges, inv_bin_widths, n_bins, col_offsets)
+    ctx.layout = int(layout)
+    ctx.total_bins = int(total_bins)
+    ctx.set_materialize_grads(False)
+
+
+def _encoding_backward(ctx: Any, grad_output):
+    if grad_output is None or not ctx.needs_input_grad[0]:
+        return (None,) * 8
+    x, bin_edges, inv_bin_widths, n_bins, col_offsets = ctx.saved_tensors
+    grad_x = torch.ops.rtdl_num_embeddings_cuda.encoding_backward(
+        grad_output.contiguous(), x, bin_edges, inv_bin_widths, n_bins, col_offsets, ctx.layout, ctx.total_bins,
+    )
+    return (grad_x,) + (None,) * 7
+
+
+torch.library.register_autograd(
+    "rtdl_num_embeddings_cuda::encoding_forward", _encoding_backward, setup_context=_setup_encoding_context,
+)

@@ -101,3 +101,26 @@ def _embeddings_backward_fake(grad_output, x, bin_edges, inv_bin_widths, n_bins,
         empty((f, d), compute_grad_linear0 and epilogue == 2),
         empty((f, d), compute_grad_linear0 and epilogue == 2),
     )
+
+
+ENC_RAGGED, ENC_PADDED = 0, 1
+
+
+@torch.library.register_fake("rtdl_num_embeddings_cuda::encoding_forward")
+def _encoding_forward_fake(x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout: int, total_bins: int,
+                           output_dtype: torch.dtype) -> Tensor:
+    torch._check(x.ndim == 2, lambda: "x must have shape [N, F]")
+    torch._check(x.dtype == torch.float32, lambda: "x must be float32")
+    torch._check(output_dtype in SUPPORTED_FLOAT_DTYPES, lambda: "Unsupported output dtype")
+    torch._check(layout in (ENC_RAGGED, ENC_PADDED), lambda: "layout must be 0 (ragged) or 1 (padded)")
+    if layout == ENC_PADDED:
+        return torch.empty((x.shape[0], x.shape[1], inv_bin_widths.shape[1]), dtype=output_dtype, device=x.device)
+    torch._check(col_offsets is not None, lambda: "the ragged layout needs col_offsets")
+    return torch.empty((x.shape[0], total_bins), dtype=output_dtype, device=x.device)
+
+
+@torch.library.register_fake("rtdl_num_embeddings_cuda::encoding_backward")
+def _encoding_backward_fake(grad_output, x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout: int,
+                            total_bins: int) -> Tensor:
+    torch._check(grad_output.shape[0] == x.shape[0], lambda: "grad_output N mismatch")
+    return torch.empty_like(x)

@@ -73,6 +73,10 @@ def capi() -> ctypes.CDLL:
     lib.ple_embeddings_backward_noalloc.restype = I
     lib.ple_embeddings_backward_noalloc.argtypes = [P, I, P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64,
                                                     P, I, P, P, P, P, P, P]
+    lib.ple_encoding_forward.restype = I
+    lib.ple_encoding_forward.argtypes = [P, P, P, P, P, I, I64, I64, I64, I64, I, P, P]
+    lib.ple_encoding_backward.restype = I
+    lib.ple_encoding_backward.argtypes = [P, I, P, P, P, P, P, I, I64, I64, I64, I64, P, P]
     _capi = lib
     return lib
 

@@ -10,6 +10,8 @@
 //            compute_grad_x, compute_grad_weight) -> (grad_x, grad_weight)
 // Added (the fused module path):
 //   embeddings_forward / embeddings_backward.
+// Added (the standalone encoding, upstream PiecewiseLinearEncoding):
+//   encoding_forward / encoding_backward.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -241,6 +243,81 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
   return {gx, gw, gb, gw0, gb0};
 }
 
+void check_encoding(const at::Tensor& x, const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
+                    const at::Tensor& n_bins, const std::optional<at::Tensor>& col_offsets, int64_t layout,
+                    int64_t total_bins) {
+  TORCH_CHECK(x.is_cuda() && bin_edges.is_cuda() && inv_bin_widths.is_cuda() && n_bins.is_cuda(),
+              "encoding tensors must be CUDA tensors");
+  TORCH_CHECK(x.device() == bin_edges.device() && x.device() == inv_bin_widths.device() &&
+                  x.device() == n_bins.device(),
+              "All encoding tensors must be on the same CUDA device");
+  TORCH_CHECK(x.dim() == 2, "x must have shape [N, F]");
+  TORCH_CHECK(x.scalar_type() == at::kFloat, "x must be float32");
+  TORCH_CHECK(x.is_contiguous() && bin_edges.is_contiguous() && inv_bin_widths.is_contiguous() &&
+                  n_bins.is_contiguous(),
+              "encoding tensors must be contiguous");
+  TORCH_CHECK(bin_edges.dim() == 2 && bin_edges.scalar_type() == at::kFloat, "bin_edges must be float32 [F, B + 1]");
+  TORCH_CHECK(inv_bin_widths.dim() == 2 && inv_bin_widths.scalar_type() == at::kFloat,
+              "inv_bin_widths must be float32 [F, B]");
+  TORCH_CHECK(n_bins.dim() == 1 && n_bins.scalar_type() == at::kInt, "n_bins must be int32 [F]");
+  const int64_t F = x.size(1), B = inv_bin_widths.size(1);
+  TORCH_CHECK(bin_edges.size(0) == F && inv_bin_widths.size(0) == F && n_bins.size(0) == F,
+              "bin tables must have n_features rows");
+  TORCH_CHECK(bin_edges.size(1) == B + 1, "bin_edges.size(1) must equal inv_bin_widths.size(1) + 1");
+  TORCH_CHECK(layout == PLE_ENC_RAGGED || layout == PLE_ENC_PADDED, "layout must be 0 (ragged) or 1 (padded)");
+  if (layout == PLE_ENC_RAGGED) {
+    TORCH_CHECK(col_offsets.has_value(), "the ragged layout needs col_offsets");
+    TORCH_CHECK(col_offsets->is_cuda() && col_offsets->device() == x.device(), "col_offsets must be on x's device");
+    TORCH_CHECK(col_offsets->scalar_type() == at::kLong && col_offsets->dim() == 1 && col_offsets->size(0) == F + 1 &&
+                    col_offsets->is_contiguous(),
+                "col_offsets must be a contiguous int64 tensor of shape [F + 1]");
+  } else {
+    TORCH_CHECK(total_bins == F * B, "the padded layout has n_features * max_n_bins columns");
+  }
+}
+
+at::Tensor ple_encoding_forward_op(const at::Tensor& x, const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
+                                   const at::Tensor& n_bins, const std::optional<at::Tensor>& col_offsets,
+                                   int64_t layout, int64_t total_bins, at::ScalarType output_dtype) {
+  check_encoding(x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout, total_bins);
+  TORCH_CHECK(to_code(output_dtype) >= 0 && to_code(output_dtype) <= PLE_DTYPE_BF16,
+              "output_dtype must be float32, float16, or bfloat16");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), F = x.size(1), B = inv_bin_widths.size(1);
+  at::Tensor out = layout == PLE_ENC_PADDED ? at::empty({N, F, B}, x.options().dtype(output_dtype))
+                                            : at::empty({N, total_bins}, x.options().dtype(output_dtype));
+  if (N == 0) return out;
+  check_status(ple_encoding_forward(x.data_ptr<float>(), bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                                    n_bins.data_ptr<int32_t>(),
+                                    col_offsets.has_value() ? col_offsets->data_ptr<int64_t>() : nullptr, (int)layout,
+                                    N, F, B, total_bins, to_code(output_dtype), out.data_ptr(), stream_of(x)),
+               "rtdl_num_embeddings_cuda::encoding_forward");
+  return out;
+}
+
+at::Tensor ple_encoding_backward_op(const at::Tensor& grad_output, const at::Tensor& x, const at::Tensor& bin_edges,
+                                    const at::Tensor& inv_bin_widths, const at::Tensor& n_bins,
+                                    const std::optional<at::Tensor>& col_offsets, int64_t layout, int64_t total_bins) {
+  check_encoding(x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout, total_bins);
+  TORCH_CHECK(grad_output.is_cuda() && grad_output.device() == x.device(), "grad_output must be on x's device");
+  TORCH_CHECK(grad_output.is_contiguous(), "grad_output must be contiguous");
+  TORCH_CHECK(to_code(grad_output.scalar_type()) >= 0 && to_code(grad_output.scalar_type()) <= PLE_DTYPE_BF16,
+              "grad_output must be float32, float16, or bfloat16");
+  const int64_t N = x.size(0), F = x.size(1), B = inv_bin_widths.size(1);
+  TORCH_CHECK(grad_output.numel() == N * total_bins && grad_output.size(0) == N,
+              "grad_output must have the encoding's shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor grad_x = at::empty({N, F}, x.options());
+  if (N == 0) return grad_x;
+  check_status(ple_encoding_backward(grad_output.data_ptr(), to_code(grad_output.scalar_type()), x.data_ptr<float>(),
+                                     bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                                     n_bins.data_ptr<int32_t>(),
+                                     col_offsets.has_value() ? col_offsets->data_ptr<int64_t>() : nullptr,
+                                     (int)layout, N, F, B, total_bins, grad_x.data_ptr<float>(), stream_of(x)),
+               "rtdl_num_embeddings_cuda::encoding_backward");
+  return grad_x;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
@@ -261,6 +338,12 @@ TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
       "int epilogue, bool activation, ScalarType compute_dtype, bool compute_grad_x, bool compute_grad_weight, bool compute_grad_bias, "
       "bool compute_grad_linear0) -> (Tensor grad_x, Tensor grad_weight, Tensor grad_bias, Tensor grad_w0, "
       "Tensor grad_b0)");
+  m.def(
+      "encoding_forward(Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, Tensor? col_offsets, "
+      "int layout, int total_bins, ScalarType output_dtype) -> Tensor");
+  m.def(
+      "encoding_backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, "
+      "Tensor? col_offsets, int layout, int total_bins) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
@@ -268,4 +351,6 @@ TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
   m.impl("backward", &ple_backward_op);
   m.impl("embeddings_forward", &ple_embeddings_forward_op);
   m.impl("embeddings_backward", &ple_embeddings_backward_op);
+  m.impl("encoding_forward", &ple_encoding_forward_op);
+  m.impl("encoding_backward", &ple_encoding_backward_op);
 }

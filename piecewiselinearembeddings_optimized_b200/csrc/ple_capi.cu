@@ -291,6 +291,63 @@ int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float
                        workspace_bytes, stream);
 }
 
+// ---------------------------------------------------------------- standalone encoding
+static int encoding_args(EncArgs& a, const float* x, const float* edges, const float* inv_w, const int32_t* n_bins,
+                         const int64_t* col_offsets, int layout, int64_t N, int64_t F, int64_t B,
+                         int64_t total_cols) {
+  if (N < 0) return set_error(PLE_ERR_SHAPE, "batch must be >= 0");
+  if (F <= 0) return set_error(PLE_ERR_SHAPE, "n_features must be positive");
+  if (B <= 0) return set_error(PLE_ERR_SHAPE, "max_n_bins must be positive");
+  if (F > (int64_t)1 << 30 || B > (int64_t)1 << 20) return set_error(PLE_ERR_OVERFLOW, "n_features or max_n_bins too large");
+  if (!edges || !inv_w || !n_bins) return set_error(PLE_ERR_INVALID_ARGUMENT, "bin_edges, inv_bin_widths and n_bins are required");
+  if (layout == PLE_ENC_PADDED) {
+    if (total_cols != F * B) return set_error(PLE_ERR_SHAPE, "padded layout: total_cols must equal n_features * max_n_bins");
+  } else if (layout == PLE_ENC_RAGGED) {
+    if (!col_offsets) return set_error(PLE_ERR_INVALID_ARGUMENT, "ragged layout needs col_offsets");
+    if (total_cols < F || total_cols > F * B)
+      return set_error(PLE_ERR_SHAPE, "ragged layout: total_cols must lie in [n_features, n_features * max_n_bins]");
+  } else {
+    return set_error(PLE_ERR_INVALID_ARGUMENT, "layout must be PLE_ENC_RAGGED or PLE_ENC_PADDED");
+  }
+  if (N > 0 && total_cols > INT64_MAX / N) return set_error(PLE_ERR_OVERFLOW, "N * total_cols overflows int64");
+  a = EncArgs{};
+  a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.col_off = col_offsets;
+  a.N = N; a.total_cols = total_cols; a.F = (int)F; a.B = (int)B; a.layout = layout;
+  return PLE_OK;
+}
+
+int ple_encoding_forward(const float* x, const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
+                         const int64_t* col_offsets, int layout, int64_t batch, int64_t n_features,
+                         int64_t max_n_bins, int64_t total_cols, int output_dtype, void* output, void* stream) {
+  g_msg[0] = 0;
+  EncArgs a;
+  int st = encoding_args(a, x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout, batch, n_features, max_n_bins,
+                         total_cols);
+  if (st) return st;
+  if (dtype_size(output_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "output dtype must be F32, F16 or BF16");
+  if (batch == 0) return PLE_OK;
+  if (!x || !output) return set_error(PLE_ERR_INVALID_ARGUMENT, "x and output are required");
+  a.out = output;
+  return launch_encoding_forward(a, output_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int ple_encoding_backward(const void* grad_output, int grad_dtype, const float* x, const float* bin_edges,
+                          const float* inv_bin_widths, const int32_t* n_bins, const int64_t* col_offsets, int layout,
+                          int64_t batch, int64_t n_features, int64_t max_n_bins, int64_t total_cols, float* grad_x,
+                          void* stream) {
+  g_msg[0] = 0;
+  EncArgs a;
+  int st = encoding_args(a, x, bin_edges, inv_bin_widths, n_bins, col_offsets, layout, batch, n_features, max_n_bins,
+                         total_cols);
+  if (st) return st;
+  if (dtype_size(grad_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad dtype must be F32, F16 or BF16");
+  if (batch == 0) return PLE_OK;
+  if (!grad_output || !x || !grad_x) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad_output, x and grad_x are required");
+  a.g = grad_output;
+  a.grad_x = grad_x;
+  return launch_encoding_backward(a, grad_dtype, static_cast<cudaStream_t>(stream));
+}
+
 int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, const float* x,
                                     const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
                                     const float* weight, const float* bias, const float* w0, const float* b0,

@@ -64,6 +64,19 @@ struct BwdArgs {
   int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4;
 };
 
+struct EncArgs {
+  const float* x;
+  const float* edges;
+  const float* inv_w;
+  const int32_t* n_bins;
+  const int64_t* col_off;  // [F + 1] column offsets (ragged layout)
+  const void* g;           // backward: grad of the encoding
+  void* out;               // forward: the encoding
+  float* grad_x;           // backward
+  int64_t N, total_cols;
+  int F, B, layout;
+};
+
 // error plumbing (ple_capi.cu)
 int set_error(int code, const char* msg);
 int set_cuda_error(cudaError_t e, const char* what);
@@ -76,5 +89,7 @@ int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cuda
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
+int launch_encoding_forward(const EncArgs& a, int output_dtype, cudaStream_t st);
+int launch_encoding_backward(const EncArgs& a, int grad_dtype, cudaStream_t st);
 
 }  // namespace ple

@@ -144,3 +144,82 @@ class CudaPiecewiseLinearEmbeddings(Base):
             x, self._cuda_bin_edges, self._cuda_inv_bin_widths, self._cuda_n_bins, self.linear.weight,
             bias, w0, b0, epilogue, self.activation is not None, compute, out_dtype,
         )
+
+
+ENCODING_RAGGED, ENCODING_PADDED = 0, 1
+
+
+class CudaPiecewiseLinearEncoding(torch.nn.Module):
+    """Drop-in CUDA counterpart of upstream ``PiecewiseLinearEncoding(bins)``.
+
+    ``forward(x [..., F] float32) -> [..., sum_i n_i]``: for each feature i the
+    ``n_i`` columns of its bins in logical order (feature-major, no padding),
+    column j holding ``t_j = (x - e_j) / w_j`` clamped to ``<= 1`` (first bin),
+    ``[0, 1]`` (middle bins), ``>= 0`` (last bin), unclamped for a single-bin
+    feature; NaN propagates.  ``padded=True`` returns ``[..., F, B]`` in the
+    embedding weights' physical layout instead (last real bin at column
+    ``B - 1``, zero padding).  The gradient with respect to x passes the clamps
+    at their bounds (``torch.clamp``'s rule).  The reference package has no
+    CUDA path for this module; here both directions are sm_100a kernels.
+    Non-CUDA inputs go to upstream's class when it is installed.
+    """
+
+    def __init__(self, bins: list[Tensor], *, padded: bool = False) -> None:
+        super().__init__()
+        from ._compat import check_bins
+
+        check_bins(bins)
+        edges, inv_w, n_bins = pad_bin_tables(bins)
+        counts = [int(e.numel() - 1) for e in bins]
+        offsets = [0]
+        for c in counts:
+            offsets.append(offsets[-1] + c)
+        self.register_buffer("_cuda_bin_edges", edges, persistent=False)
+        self.register_buffer("_cuda_inv_bin_widths", inv_w, persistent=False)
+        self.register_buffer("_cuda_n_bins", n_bins, persistent=False)
+        self.register_buffer("_cuda_col_offsets", torch.tensor(offsets, dtype=torch.int64, device=edges.device),
+                             persistent=False)
+        self.padded = bool(padded)
+        self.total_n_bins = offsets[-1]
+        self.max_n_bins = int(inv_w.shape[1])
+        self.output_dtype: torch.dtype = torch.float32
+        self._upstream = None
+        self._bins = [b.detach().clone() for b in bins]
+
+    @property
+    def n_features(self) -> int:
+        return int(self._cuda_n_bins.shape[0])
+
+    def _cpu_forward(self, x: Tensor) -> Tensor:
+        from . import _compat
+
+        if not getattr(_compat, "HAVE_UPSTREAM", False):
+            raise RuntimeError(
+                "CudaPiecewiseLinearEncoding has no CPU implementation; install rtdl_num_embeddings for CPU inputs"
+            )
+        if self._upstream is None:
+            from rtdl_num_embeddings import PiecewiseLinearEncoding  # pragma: no cover
+
+            self._upstream = PiecewiseLinearEncoding([b.to(x.device) for b in self._bins])  # pragma: no cover
+        return self._upstream(x)  # pragma: no cover
+
+    def forward(self, x: Tensor) -> Tensor:
+        if x.ndim < 2:
+            raise ValueError("The input must have at least two dimensions: [..., n_features]")
+        if x.shape[-1] != self.n_features:
+            raise ValueError(f"Expected {self.n_features} numerical features, got {x.shape[-1]}")
+        if x.device.type != "cuda":
+            return self._cpu_forward(x)
+        if x.device != self._cuda_bin_edges.device:
+            raise RuntimeError("x and the module must be on the same CUDA device")
+        if x.dtype != torch.float32:
+            raise TypeError(f"The CUDA encoding requires float32 x. Got {x.dtype}.")
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.n_features).contiguous()
+        layout = ENCODING_PADDED if self.padded else ENCODING_RAGGED
+        total = self.n_features * self.max_n_bins if self.padded else self.total_n_bins
+        y = torch.ops.rtdl_num_embeddings_cuda.encoding_forward(
+            x2, self._cuda_bin_edges, self._cuda_inv_bin_widths, self._cuda_n_bins, self._cuda_col_offsets, layout,
+            total, self.output_dtype,
+        )
+        return y.reshape(*lead, *y.shape[1:])

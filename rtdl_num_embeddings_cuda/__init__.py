@@ -11,8 +11,11 @@ from piecewiselinearembeddings_optimized_b200 import _native
 _native.load_ops()
 from piecewiselinearembeddings_optimized_b200 import _meta as _meta  # noqa: E402,F401
 from piecewiselinearembeddings_optimized_b200 import _autograd as _autograd  # noqa: E402,F401
-from piecewiselinearembeddings_optimized_b200.module import CudaPiecewiseLinearEmbeddings  # noqa: E402
+from piecewiselinearembeddings_optimized_b200.module import (  # noqa: E402
+    CudaPiecewiseLinearEmbeddings,
+    CudaPiecewiseLinearEncoding,
+)
 
-__all__ = ["CudaPiecewiseLinearEmbeddings"]
+__all__ = ["CudaPiecewiseLinearEmbeddings", "CudaPiecewiseLinearEncoding"]
 
 __version__ = "0.2.0.dev0+b200"
