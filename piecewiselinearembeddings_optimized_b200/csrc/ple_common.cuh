@@ -184,6 +184,7 @@ __host__ __device__ __forceinline__ int physical_bin(int k, int n_real, int max_
 __device__ __forceinline__ float relu_f(float v) { return v <= 0.0f ? 0.0f : v; }
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 template <typename T>
 __host__ __device__ __forceinline__ T ceil_div(T a, T b) {

@@ -116,68 +116,140 @@ __global__ void __launch_bounds__(kEncThreads) ple_enc_fwd_kernel(const EncArgs 
   ColInfo ci[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) ci[e] = sc[q0 + e];
-  for (int64_t s = blockIdx.y; s < a.N; s += gridDim.y) {
-    const float* xrow = a.x + s * a.F;
-    float v[4];
+  // the common case: the four columns belong to one feature (n_i >= 4), so one x per row; four rows per
+  // iteration with their loads issued first
+  const bool one_f = ci[0].f >= 0 && ci[1].f == ci[0].f && ci[2].f == ci[0].f && ci[3].f == ci[0].f;
+  for (int64_t s = (int64_t)blockIdx.y * 4; s < a.N; s += (int64_t)gridDim.y * 4) {
+    const int nrow = (int)min64(4, a.N - s);
+    if (one_f) {
+      float xv[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[e] = 0.f;
-      if (ci[e].f >= 0) v[e] = clamp_keep_nan((__ldg(xrow + ci[e].f) - ci[e].e) * ci[e].r, ci[e].lo, ci[e].hi);
+      for (int r = 0; r < 4; ++r) xv[r] = r < nrow ? __ldg(a.x + (s + r) * a.F + ci[0].f) : 0.f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (r < nrow) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = clamp_keep_nan((xv[r] - ci[e].e) * ci[e].r, ci[e].lo, ci[e].hi);
+          store4<OT>(out + (s + r) * C + c0 + q0, v, vec_ok, valid);
+        }
+      }
+    } else {
+      for (int r = 0; r < nrow; ++r) {
+        const float* xrow = a.x + (s + r) * a.F;
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[e] = 0.f;
+          if (ci[e].f >= 0) v[e] = clamp_keep_nan((__ldg(xrow + ci[e].f) - ci[e].e) * ci[e].r, ci[e].lo, ci[e].hi);
+        }
+        store4<OT>(out + (s + r) * C + c0 + q0, v, vec_ok, valid);
+      }
     }
-    store4<OT>(out + s * C + c0 + q0, v, vec_ok, valid);
   }
 }
 
-// Backward: CTA = (kBwdRows rows) x (feature group of fg features).  The rows'
-// gradient segment of the group is staged in shared memory with coalesced
-// loads, then each (row, feature) pair sums its columns.
+// Four consecutive gradients (aligned to four elements) as fp32.
+template <typename GT>
+__device__ __forceinline__ void load4(const GT* p, float (&v)[4]) {
+  if constexpr (std::is_same<GT, float>::value) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+  } else {
+    const uint2 q = __ldg(reinterpret_cast<const uint2*>(p));
+    const GT* h = reinterpret_cast<const GT*>(&q);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = Dt<GT>::to_f(h[e]);
+  }
+}
+
+// Backward: blockIdx.x = feature group (at most kEncGroupCols columns; its
+// column table is built once), blockIdx.y strides over blocks of kEncBwdRows
+// rows.  Per block, threads take the group's columns of each row in order
+// (coalesced gradient loads) and stage each column's contribution
+// g * r * [lo <= t <= hi] in shared memory; then each (row, feature) sums its
+// columns.
 constexpr int kEncBwdRows = 8;
+constexpr int kEncGroupCols = 2048;
 
 template <typename GT>
 __global__ void __launch_bounds__(kEncThreads) ple_enc_bwd_kernel(const EncArgs a, int fg, int pitch) {
-  extern __shared__ float sg[];  // [kEncBwdRows][pitch]
+  extern __shared__ float smem_f[];
+  ColInfo* sc = reinterpret_cast<ColInfo*>(smem_f);                // [pitch] column table of the group
+  float* sv = smem_f + (size_t)pitch * (sizeof(ColInfo) / 4);       // [kEncBwdRows][pitch] contributions
+  float* sx = sv + (size_t)kEncBwdRows * pitch;                     // [kEncBwdRows][fg] x of the block
   const int64_t C = a.total_cols;
   const GT* g = reinterpret_cast<const GT*>(a.g);
-  const int n_groups = (a.F + fg - 1) / fg;
+  const int grp = blockIdx.x;
+  const int f_lo = grp * fg, f_hi = min(a.F, f_lo + fg);
+  const int64_t cb = a.layout == PLE_ENC_PADDED ? (int64_t)f_lo * a.B : a.col_off[f_lo];
+  const int64_t ce = a.layout == PLE_ENC_PADDED ? (int64_t)f_hi * a.B : a.col_off[f_hi];
+  // width bounded by the buffers and the row even if the offsets disagree with n_bins
+  const int w = (cb < 0 || cb > C) ? 0 : (int)min64(min64(ce - cb, (int64_t)pitch - 1), C - cb);
+  for (int c = threadIdx.x; c < w; c += blockDim.x) {
+    ColInfo ci = column_info(a, cb + c);
+    if (ci.f < f_lo || ci.f >= f_hi) ci.f = -1;  // (only with inconsistent offsets)
+    sc[c] = ci;
+  }
+  const int nf = f_hi - f_lo;
+  // vector loads of four gradients need every chunk start aligned: row length, group start and base
+  const bool vec_g = ((C | cb) & 3) == 0 && (reinterpret_cast<uintptr_t>(g) & (4 * sizeof(GT) - 1)) == 0;
   const int64_t row_blocks = (a.N + kEncBwdRows - 1) / kEncBwdRows;
-  for (int64_t work = blockIdx.x; work < (int64_t)n_groups * row_blocks; work += gridDim.x) {
-    const int grp = (int)(work % n_groups);
-    const int64_t rb = work / n_groups;
-    const int f_lo = grp * fg, f_hi = min(a.F, f_lo + fg);
-    const int64_t cb = a.layout == PLE_ENC_PADDED ? (int64_t)f_lo * a.B : a.col_off[f_lo];
-    const int64_t ce = a.layout == PLE_ENC_PADDED ? (int64_t)f_hi * a.B : a.col_off[f_hi];
-    // staged width, bounded by the buffer and the row even if the offsets disagree with n_bins
-    const int w = (cb < 0 || cb > C) ? 0 : (int)min64(min64(ce - cb, (int64_t)pitch - 1), C - cb);
+  for (int64_t rb = blockIdx.y; rb < row_blocks; rb += gridDim.y) {
     const int64_t s0 = rb * kEncBwdRows;
     const int nr = (int)min64(kEncBwdRows, a.N - s0);
-    __syncthreads();  // previous work item finished with the staged rows
-    for (int rr = 0; rr < nr; ++rr) {
-      const GT* grow = g + (s0 + rr) * C + cb;
-      for (int c = threadIdx.x; c < w; c += blockDim.x) sg[rr * pitch + c] = Dt<GT>::to_f(grow[c]);
+    __syncthreads();  // column table ready / previous block's sums done
+    for (int p = threadIdx.x; p < nr * nf; p += blockDim.x) {
+      const int rr = p / nf, i = p - rr * nf;
+      sx[rr * fg + i] = a.x[(s0 + rr) * a.F + f_lo + i];
     }
     __syncthreads();
-    const int nf = f_hi - f_lo;
+    // four columns per thread and chunk; the chunk's gradients of all the block's rows are loaded before any
+    // is used (the loads would otherwise serialise behind the shared-memory stores)
+    const int nchunks = (w + 3) >> 2;
+    for (int q = threadIdx.x; q < nchunks; q += blockDim.x) {
+      const int c = q << 2;
+      const int cn = min(4, w - c);
+      float gv[kEncBwdRows][4];
+#pragma unroll
+      for (int rr = 0; rr < kEncBwdRows; ++rr) {
+        if (rr < nr) {
+          const GT* gp = g + (s0 + rr) * C + cb + c;
+          if (vec_g && cn == 4) {
+            load4<GT>(gp, gv[rr]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) gv[rr][e] = e < cn ? Dt<GT>::to_f(gp[e]) : 0.f;
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (e < cn) {
+          const ColInfo ci = sc[c + e];
+#pragma unroll
+          for (int rr = 0; rr < kEncBwdRows; ++rr) {
+            if (rr < nr) {
+              float v = 0.f;
+              if (ci.f >= 0) {
+                const float t = (sx[rr * fg + ci.f - f_lo] - ci.e) * ci.r;
+                if (t >= ci.lo && t <= ci.hi) v = gv[rr][e] * ci.r;
+              }
+              sv[rr * pitch + c + e] = v;
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
     for (int p = threadIdx.x; p < nr * nf; p += blockDim.x) {
       const int rr = p % nr, i = f_lo + p / nr;  // rows fastest: lanes of a feature read different rows
-      const float xv = a.x[(s0 + rr) * a.F + i];
-      const int n = a.n_bins[i];
-      const float* er = a.edges + (int64_t)i * (a.B + 1);
-      const float* rw = a.inv_w + (int64_t)i * a.B;
-      const int off = (int)((a.layout == PLE_ENC_PADDED ? (int64_t)i * a.B : a.col_off[i]) - cb);
-      const float* row = sg + rr * pitch + off;
-      // columns of this feature inside the staged width (all of them for consistent offsets)
-      const int span = a.layout == PLE_ENC_PADDED ? a.B : n;
-      const int nn = (off < 0 || off + span > w || n > a.B) ? 0 : n;
-      const float inf = __int_as_float(0x7f800000);
+      const int64_t c_i = a.layout == PLE_ENC_PADDED ? (int64_t)i * a.B : a.col_off[i];
+      const int64_t c_n = a.layout == PLE_ENC_PADDED ? c_i + a.B : a.col_off[i + 1];
+      const int lo = (int)max64(0, c_i - cb), hi = (int)min64(w, c_n - cb);
+      const float* row = sv + rr * pitch;
       float acc = 0.f;
-      for (int j = 0; j < nn; ++j) {
-        const int col = (a.layout == PLE_ENC_PADDED && j == n - 1) ? a.B - 1 : j;
-        const float r = rw[j];
-        const float t = (xv - er[j]) * r;
-        const float lo = (n == 1 || j == 0) ? -inf : 0.f;
-        const float hi = (n == 1 || j == n - 1) ? inf : 1.f;
-        if (t >= lo && t <= hi) acc = fmaf(row[col], r, acc);
-      }
+      for (int c = lo; c < hi; ++c) acc += row[c];
       a.grad_x[(s0 + rr) * a.F + i] = acc;
     }
   }
@@ -196,16 +268,19 @@ int launch_enc_fwd_t(const EncArgs& a, cudaStream_t st) {
 
 template <typename GT>
 int launch_enc_bwd_t(const EncArgs& a, cudaStream_t st) {
-  // feature groups of at most 2048 staged columns (B bounds a feature's columns)
-  const int fg = (int)(a.B >= 2048 ? 1 : 2048 / a.B);
+  // feature groups of at most kEncGroupCols columns (B bounds a feature's columns)
+  const int fg = (int)(a.B >= kEncGroupCols ? 1 : kEncGroupCols / a.B);
   const int64_t wmax = (int64_t)fg * a.B;
   const int pitch = (int)(wmax | 1);  // odd pitch: rows start on different banks
-  const size_t smem = (size_t)kEncBwdRows * pitch * sizeof(float);
+  const size_t smem = (size_t)pitch * (sizeof(ColInfo) + kEncBwdRows * sizeof(float)) +
+                      (size_t)kEncBwdRows * fg * sizeof(float);
   auto kern = ple_enc_bwd_kernel<GT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(encoding backward)");
-  const int64_t work = (int64_t)((a.F + fg - 1) / fg) * ((a.N + kEncBwdRows - 1) / kEncBwdRows);
-  const int grid = (int)min64(work, 4L * device_sm_count());
+  const int n_groups = (a.F + fg - 1) / fg;
+  const int64_t row_blocks = (a.N + kEncBwdRows - 1) / kEncBwdRows;
+  const int64_t per_group = min64(min64(row_blocks, 65535), ceil_div<int64_t>(4L * device_sm_count(), n_groups));
+  dim3 grid((unsigned)n_groups, (unsigned)(per_group < 1 ? 1 : per_group));
   kern<<<grid, kEncThreads, smem, st>>>(a, fg, pitch);
   e = cudaGetLastError();
   return e == cudaSuccess ? PLE_OK : set_cuda_error(e, "encoding backward launch");
