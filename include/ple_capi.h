@@ -230,6 +230,21 @@ int ple_encoding_backward(const void* grad_output, int grad_dtype, const float* 
                           int64_t batch, int64_t n_features, int64_t max_n_bins,
                           int64_t total_cols, float* grad_x, void* stream);
 
+/*
+ * Quantile bin edges on the device (upstream rtdl_num_embeddings.compute_bins
+ * without a tree; the reference builds its tables on the host,
+ * module.py:58-109).  sorted_columns[F][n_rows]: each feature's training
+ * column sorted ascending (n_rows >= 2, finite).  For every feature the
+ * quantiles at j / n_bins (j = 0..n_bins), linearly interpolated between order
+ * statistics, with repeated values removed, are written as
+ *   bin_edges[F][n_bins + 1]   (+inf after the n_i + 1 distinct edges),
+ *   inv_bin_widths[F][n_bins]  (1 / (e_{j+1} - e_j), 0 padding),
+ *   n_bins_out[F]              (n_i = distinct edges - 1; 0 for a constant column).
+ * 1 <= n_bins <= 1023.
+ */
+int ple_compute_bins(const float* sorted_columns, int64_t n_rows, int64_t n_features, int n_bins,
+                     float* bin_edges, float* inv_bin_widths, int32_t* n_bins_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

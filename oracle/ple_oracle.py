@@ -446,3 +446,14 @@ def encoding_grad_x(g, x, edges, inv_w, n_bins, *, padded=False):
             ab[:, i] += np.abs(term)
         c += nb
     return gx, ab
+
+
+# ---------------------------------------------------------------- bin edges
+
+def quantile_bins(X, n_bins):
+    """Quantile bin edges per feature (upstream ``compute_bins`` without a
+    tree): ``unique(quantile(X[:, i], linspace(0, 1, n_bins + 1)))`` with
+    linear interpolation, in float64."""
+    X = np.asarray(X, dtype=np.float64)
+    qs = np.linspace(0.0, 1.0, n_bins + 1)
+    return [np.unique(np.quantile(X[:, i], qs, method="linear")) for i in range(X.shape[1])]

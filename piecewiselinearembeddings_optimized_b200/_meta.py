@@ -124,3 +124,12 @@ def _encoding_backward_fake(grad_output, x, bin_edges, inv_bin_widths, n_bins, c
                             total_bins: int) -> Tensor:
     torch._check(grad_output.shape[0] == x.shape[0], lambda: "grad_output N mismatch")
     return torch.empty_like(x)
+
+
+@torch.library.register_fake("rtdl_num_embeddings_cuda::compute_bins")
+def _compute_bins_fake(x, n_bins: int):
+    torch._check(x.ndim == 2, lambda: "x must have shape [N, F]")
+    f = x.shape[1]
+    return (torch.empty((f, n_bins + 1), dtype=torch.float32, device=x.device),
+            torch.empty((f, n_bins), dtype=torch.float32, device=x.device),
+            torch.empty((f,), dtype=torch.int32, device=x.device))

@@ -77,6 +77,8 @@ def capi() -> ctypes.CDLL:
     lib.ple_encoding_forward.argtypes = [P, P, P, P, P, I, I64, I64, I64, I64, I, P, P]
     lib.ple_encoding_backward.restype = I
     lib.ple_encoding_backward.argtypes = [P, I, P, P, P, P, P, I, I64, I64, I64, I64, P, P]
+    lib.ple_compute_bins.restype = I
+    lib.ple_compute_bins.argtypes = [P, I64, I64, I, P, P, P, P]
     _capi = lib
     return lib
 

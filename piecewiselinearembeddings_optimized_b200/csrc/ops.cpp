@@ -318,6 +318,22 @@ at::Tensor ple_encoding_backward_op(const at::Tensor& grad_output, const at::Ten
   return grad_x;
 }
 
+std::tuple<at::Tensor, at::Tensor, at::Tensor> ple_compute_bins_op(const at::Tensor& x, int64_t n_bins) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kFloat, "x must be a float32 CUDA tensor [N, F]");
+  TORCH_CHECK(x.size(0) >= 2, "compute_bins needs at least two rows");
+  TORCH_CHECK(n_bins >= 1 && n_bins <= 1023, "n_bins must lie in [1, 1023]");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), F = x.size(1);
+  at::Tensor sorted = std::get<0>(at::sort(x.t().contiguous(), 1));  // [F, N], each column ascending
+  at::Tensor edges = at::empty({F, n_bins + 1}, x.options());
+  at::Tensor inv_w = at::empty({F, n_bins}, x.options());
+  at::Tensor nb = at::empty({F}, x.options().dtype(at::kInt));
+  check_status(ple_compute_bins(sorted.data_ptr<float>(), N, F, (int)n_bins, edges.data_ptr<float>(),
+                                inv_w.data_ptr<float>(), nb.data_ptr<int32_t>(), stream_of(x)),
+               "rtdl_num_embeddings_cuda::compute_bins");
+  return {edges, inv_w, nb};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
@@ -344,6 +360,7 @@ TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
   m.def(
       "encoding_backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, "
       "Tensor? col_offsets, int layout, int total_bins) -> Tensor");
+  m.def("compute_bins(Tensor x, int n_bins) -> (Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins)");
 }
 
 TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
@@ -353,4 +370,5 @@ TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
   m.impl("embeddings_backward", &ple_embeddings_backward_op);
   m.impl("encoding_forward", &ple_encoding_forward_op);
   m.impl("encoding_backward", &ple_encoding_backward_op);
+  m.impl("compute_bins", &ple_compute_bins_op);
 }

@@ -348,6 +348,19 @@ int ple_encoding_backward(const void* grad_output, int grad_dtype, const float* 
   return launch_encoding_backward(a, grad_dtype, static_cast<cudaStream_t>(stream));
 }
 
+int ple_compute_bins(const float* sorted_columns, int64_t n_rows, int64_t n_features, int n_bins, float* bin_edges,
+                     float* inv_bin_widths, int32_t* n_bins_out, void* stream) {
+  g_msg[0] = 0;
+  if (n_rows < 2) return set_error(PLE_ERR_SHAPE, "compute_bins needs at least two rows");
+  if (n_features <= 0) return set_error(PLE_ERR_SHAPE, "n_features must be positive");
+  if (n_features > 0x7fffffff) return set_error(PLE_ERR_OVERFLOW, "n_features too large");
+  if (n_bins < 1 || n_bins > 1023) return set_error(PLE_ERR_UNSUPPORTED, "n_bins must lie in [1, 1023]");
+  if (!sorted_columns || !bin_edges || !inv_bin_widths || !n_bins_out)
+    return set_error(PLE_ERR_INVALID_ARGUMENT, "compute_bins: every pointer is required");
+  return launch_bins(sorted_columns, n_rows, n_features, n_bins + 1, bin_edges, inv_bin_widths, n_bins_out, n_bins + 1,
+                     static_cast<cudaStream_t>(stream));
+}
+
 int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, const float* x,
                                     const float* bin_edges, const float* inv_bin_widths, const int32_t* n_bins,
                                     const float* weight, const float* bias, const float* w0, const float* b0,

@@ -91,5 +91,7 @@ int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
 int launch_encoding_forward(const EncArgs& a, int output_dtype, cudaStream_t st);
 int launch_encoding_backward(const EncArgs& a, int grad_dtype, cudaStream_t st);
+int launch_bins(const float* sorted, int64_t N, int64_t F, int n_q, float* edges, float* inv_w, int32_t* n_bins,
+                int ld_e, cudaStream_t st);
 
 }  // namespace ple

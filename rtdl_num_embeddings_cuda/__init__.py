@@ -16,6 +16,8 @@ from piecewiselinearembeddings_optimized_b200.module import (  # noqa: E402
     CudaPiecewiseLinearEncoding,
 )
 
-__all__ = ["CudaPiecewiseLinearEmbeddings", "CudaPiecewiseLinearEncoding"]
+from piecewiselinearembeddings_optimized_b200.bins import bin_tables, compute_bins  # noqa: E402
+
+__all__ = ["CudaPiecewiseLinearEmbeddings", "CudaPiecewiseLinearEncoding", "compute_bins", "bin_tables"]
 
 __version__ = "0.2.0.dev0+b200"
