@@ -677,9 +677,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
           const unsigned act = __ballot_sync(0xffffffffu, v);
           if (v) {
             const int k = L.sKey[(my_i << lgSt) + s];
-            // lanes with the same bin: intersect the ballots of every bin bit (pow2 > every bin)
+            // lanes with the same bin: intersect the ballots of every bin bit (bins are < B)
             unsigned peers = act;
-            for (int bit = 1; bit < a.pow2; bit <<= 1) {
+            for (int bit = 1; bit < B; bit <<= 1) {
               const unsigned bal = __ballot_sync(act, k & bit);
               peers &= (k & bit) ? bal : ~bal;
             }
