@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 3
+#define PLE_ABI_VERSION 4
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -77,6 +77,26 @@ int ple_abi_version(void);
 
 /* Static description of a status code. */
 const char* ple_status_string(int status);
+
+/*
+ * Backward kernels.  ple_backward and ple_embeddings_backward run the sorted
+ * kernel (a per-tile counting sort by bin and a segmented walk).  With the
+ * environment variable PLE_BACKWARD_KERNEL=tensor they run the tensor-core
+ * kernel instead (per-bin sums as one-hot GEMMs on tcgen05, exact bf16 part
+ * splits, TMEM accumulators), which covers max_n_bins <= 128, d_embedding a
+ * multiple of 8 up to 32 and the shapes whose tiles fit, and returns
+ * PLE_ERR_UNSUPPORTED elsewhere.  Both are deterministic and give the same
+ * results within the fp32 summation tolerance; the sorted kernel is the faster
+ * one on the measured configurations.
+ *
+ * Status word of the tensor-core backward on the current device: 1 if one of
+ * its waits for the tensor core ran past its iteration limit since the last
+ * call (that launch then skipped its remaining work, so its gradients are
+ * incomplete, and released its tensor memory), 0 if not, -1 if the word could
+ * not be read.  Reading clears it.  Synchronous (a device-to-host copy).
+ * No counterpart in the reference.
+ */
+int ple_tensor_core_status(void);
 
 /* Detail message of the last failing call on the calling host thread. */
 const char* ple_last_error_message(void);

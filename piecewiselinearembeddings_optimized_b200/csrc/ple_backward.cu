@@ -1,9 +1,17 @@
 // ple_backward.cu - planning, workspace and finalize of the fused PLE backward
 // (the kernel itself is in ple_backward_impl.cuh, instantiated per dtype pair
 // in ple_backward_<dtypes>.cu so that the instantiations compile in parallel).
-#include "ple_backward_impl.cuh"
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "ple_backward_tc.cuh"
 
 namespace ple {
+
+// Set to 1 by a tensor-core backward whose wait expired (ple_tensor_core_status reads and clears it).
+__device__ int g_tc_dev_err = 0;
 
 int launch_bwd_f32(const BwdArgs& a, int vec, cudaStream_t st);
 int launch_bwd_bf16(const BwdArgs& a, int vec, cudaStream_t st);
@@ -15,7 +23,7 @@ int launch_bwd_f16_f32(const BwdArgs& a, int vec, cudaStream_t st);
 // CTA order (deterministic).  Rows whose gradient was not requested are
 // neither read nor written.
 __global__ void ple_bwd_finalize_kernel(const BwdArgs a, int grid) {
-  const int B = a.B, D = a.D, lgFc = a.lgFc, Fc = 1 << lgFc;
+  const int B = a.B, D = a.D, Fc = a.Fc;
   const int64_t rows = (int64_t)a.F * (B + 3) * D;
   const int64_t total = (int64_t)a.n_chunks * a.N;
   const int64_t slot = (int64_t)Fc * (B + 3) * D;
@@ -29,7 +37,7 @@ __global__ void ple_bwd_finalize_kernel(const BwdArgs a, int grid) {
                : row == B + 1 ? (a.grad_w0 ? a.grad_w0 + f * D + d : nullptr)
                               : (a.grad_b0 ? a.grad_b0 + f * D + d : nullptr);
     if (dst == nullptr) continue;
-    const int chunk = (int)(f >> lgFc), i = (int)(f & (Fc - 1));
+    const int chunk = (int)(f / Fc), i = (int)(f - (int64_t)chunk * Fc);
     const int64_t c_lo = (int64_t)chunk * a.N, c_hi = c_lo + a.N;
     // first CTA whose range [total*j/grid, total*(j+1)/grid) ends past the chunk start
     int64_t j = c_lo * grid / total;
@@ -89,6 +97,7 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
         a.lgWf = lgWf;
         a.lgSt = lgSt;
         a.n_chunks = (int)ceil_div<int64_t>(a.F, Fc);
+        a.Fc = Fc;
         *smem_out = bytes;
       }
       break;
@@ -119,7 +128,19 @@ size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
   if (!bwd_plan(b, backward_vec(D, 4), &smem)) return 0;
   int grid = 0;
   bwd_grid(b, &grid);
-  return ws_bytes_for(b, grid);
+  size_t bytes = ws_bytes_for(b, grid);
+  // the tensor-core kernel's needs for each compute type (parts of q(g') and of q(t) q(g'))
+  // (bf16 parts of H, of U, register cap) per (compute, gradient) type pair
+  const int parts[5][3] = {{3, 3, tc_max_regs<float>()}, {1, 2, tc_max_regs<__nv_bfloat16>()},
+                           {1, 2, tc_max_regs<float>()}, {2, 3, tc_max_regs<__half>()}, {2, 3, tc_max_regs<float>()}};
+  for (const auto& pp : parts) {
+    BwdArgs t{};
+    t.N = N; t.F = (int)F; t.B = (int)B; t.D = (int)D;
+    TcGeom m{};
+    int threads = 0, tg = 0;
+    if (tc_plan(t, pp[0], pp[1], tc_max_warps(pp[2]), &m, &threads, &smem)) bytes = std::max(bytes, tc_ws_floats(t, m, threads, &tg) * 4);
+  }
+  return bytes;
 }
 
 int bwd_prepare(BwdArgs& a, int vec, size_t* smem, int* grid) {
@@ -129,6 +150,148 @@ int bwd_prepare(BwdArgs& a, int vec, size_t* smem, int* grid) {
     return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
   a.x_vec4 = ((1 << a.lgFc) >= 4) && (a.F % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
   return PLE_OK;
+}
+
+// ------------------------------------------------------------ tensor-core kernel planning
+static int pow2_at_least(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+static size_t tc_layout(TcGeom& m, int B, int D, int pow2) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 127) & ~(size_t)127;
+    return (int)o;
+  };
+  const int units = m.nG * m.nh;
+  m.oA = take((size_t)2 * m.nG * 128 * m.R * 2);
+  m.oB = take((size_t)2 * m.nG * m.R * m.cols * 2);  // directly after A (zeroed together)
+  m.oT = take((size_t)B * m.ts * 4);
+  m.oS = take((size_t)B * m.ts * 4);
+  m.oE = take((size_t)pow2 * m.Fc * 4);
+  m.oR = take((size_t)B * m.Fc * 4);
+  m.oN = take((size_t)m.Fc * 4);
+  m.oGX = take((size_t)2 * m.R * m.Fc * m.nh * 4);  // [2][Fc * nh][R]
+  m.oTot = take((size_t)units * 4 * 8 * 4);
+  m.oKey = take((size_t)2 * m.R * m.Fc);
+  m.oBar = take(64);  // full[2], empty[2], TMEM address, non-finite flag, abort flag
+  (void)D;
+  return off;
+}
+
+// Geometry of the tensor-core kernel, false where it does not apply: bins <= 128 (padded to Bp = 32,
+// 64 or 128; FM = 128 / Bp features share an MMA's M = 128 rows), D a multiple of 8 up to 32 (one
+// warp of flush lanes per 8-column block and group), one feature's parts * D columns <= 256 (one MMA).
+bool tc_plan(const BwdArgs& a, int parts_h, int parts_u, int max_warps, TcGeom* m, int* threads, size_t* smem) {
+  const int B = a.B, D = a.D;
+  if (B < 1 || B > 128 || D % 8 != 0 || D > 32 || a.F < 1) return false;
+  int Bp = 32;
+  while (Bp < B) Bp <<= 1;
+  const int Cf = (parts_h + parts_u) * D;
+  if (Cf > 256) return false;
+  const int nh = D / 8;
+  const int pow2 = pow2_at_least(B + 1);
+  int lgp = 0;
+  while ((1 << lgp) < pow2) ++lgp;
+  const size_t optin = device_max_smem_optin();
+  // FM features stacked in the M = 128 rows (up to 128 / Bp; rows past FM * Bp stay zero), nG groups of
+  // accumulators plus 16 running-sum columns per unit (group, column block) in TMEM: the most of both whose
+  // producer warps and shared memory fit
+  for (int FM = 128 / Bp; FM >= 1; FM >>= 1) {
+    int fpm = FM;
+    while (fpm > 1 && fpm * Cf > 256) fpm >>= 1;
+    const int Nmma = (fpm * Cf + 15) & ~15;
+    const int n_mma = FM / fpm, cols = n_mma * Nmma;
+    int nG = kTcTmemCols / (cols + 16 * nh);
+    nG = std::min<int>(nG, (int)ceil_div<int64_t>(a.F, FM));
+    for (; nG >= 1; --nG) {
+      TcGeom g{};
+      g.Bp = Bp; g.FM = FM; g.fpm = fpm; g.Nmma = Nmma; g.n_mma = n_mma; g.cols = cols; g.nG = nG; g.nh = nh;
+      g.Fc = nG * FM;
+      g.ts = table_stride(g.Fc, D);
+      g.lgp = lgp;
+      // producer warps: a multiple of the (feature, column block) count C (each warp keeps one) and of 4
+      // (the TMEM lane quarters); each warp drains nu of the nG * nh units
+      const int C = g.Fc * nh;
+      int WP = C;
+      while (WP % 4) WP += C;
+      if (WP * 32 > kTcMaxProducers || WP + 1 > max_warps || (4 * nG * nh) % WP != 0) continue;
+      g.nu = 4 * nG * nh / WP;
+      g.R = 32 * kTcItems * WP / C;
+      size_t bytes = tc_layout(g, B, D, pow2);
+      // more than half of an SM's shared memory: one CTA per SM, so the 512-column TMEM allocation never waits
+      bytes = std::max<size_t>(bytes, 116 * 1024);
+      if (bytes > optin) continue;
+      g.flush_tiles = std::max(1, 256 / g.R);  // the accumulators are drained every 256 samples
+      *m = g;
+      *threads = 32 * WP;
+      *smem = bytes;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Workspace floats of the tensor-core kernel: partials [grid][max_segs][Fc][B + 3][D], non-finite sums
+// [grid][Fc][Bp][2][D], epilogue scratch [grid][threads][16]; fills a's chunking and m's offsets.
+size_t tc_ws_floats(BwdArgs& a, TcGeom& m, int threads, int* grid) {
+  a.Fc = m.Fc;
+  a.n_chunks = (int)ceil_div<int64_t>(a.F, m.Fc);
+  const int64_t total = (int64_t)a.n_chunks * a.N;
+  int64_t g = device_sm_count();
+  const int64_t min_units = 64;
+  if (g > total / min_units) g = total / min_units;
+  if (g < 1) g = 1;
+  *grid = (int)g;
+  const int64_t len = ceil_div<int64_t>(total, g);
+  a.max_segs = (int)(ceil_div<int64_t>(len, a.N) + 1);
+  const int64_t partials = g * a.max_segs * (int64_t)m.Fc * (a.B + 3) * a.D;
+  m.spec_off = (partials + 63) & ~(int64_t)63;
+  const int64_t spec = g * (int64_t)m.Fc * m.Bp * 2 * a.D;
+  m.escr_off = (m.spec_off + spec + 63) & ~(int64_t)63;
+  return (size_t)(m.escr_off + g * (int64_t)threads * 16);
+}
+
+static int* tc_err_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  static int* cache[64] = {};
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tc_dev_err) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+int tc_prepare(BwdArgs& a, TcGeom& m, int threads, int* grid) {
+  a.pow2 = pow2_at_least(a.B + 1);
+  const size_t floats = tc_ws_floats(a, m, threads, grid);
+  if (floats * 4 > a.ws_bytes)
+    return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
+  m.dev_err = tc_err_ptr();
+  if (!m.dev_err) return set_error(PLE_ERR_CUDA, "tensor-core backward: status word not addressable");
+  return PLE_OK;
+}
+
+int tensor_core_status() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_tc_dev_err, sizeof(int)) != cudaSuccess) return -1;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_tc_dev_err, &zero, sizeof(int));
+  }
+  return v;
+}
+
+// PLE_BACKWARD_KERNEL: "tensor" selects the tensor-core backward, anything else the sorted one.
+int backward_kernel_mode() {
+  const char* v = getenv("PLE_BACKWARD_KERNEL");
+  return (v != nullptr && strcmp(v, "tensor") == 0) ? 2 : 1;
 }
 
 int bwd_finalize(const BwdArgs& a, int grid, cudaStream_t st) {

@@ -131,6 +131,8 @@ extern "C" {
 
 int ple_abi_version(void) { return PLE_ABI_VERSION; }
 
+int ple_tensor_core_status(void) { return tensor_core_status(); }
+
 const char* ple_status_string(int status) {
   switch (status) {
     case PLE_OK: return "ok";

@@ -60,8 +60,8 @@ struct BwdArgs {
   int64_t N;
   int F, B, D;
   int epi, relu;
-  // filled by the launcher
-  int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4;
+  // filled by the launcher (Fc = features per chunk; the sorted kernel uses 1 << lgFc)
+  int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4, Fc;
 };
 
 struct EncArgs {
@@ -89,6 +89,7 @@ int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cuda
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
+int tensor_core_status();
 int launch_encoding_forward(const EncArgs& a, int output_dtype, cudaStream_t st);
 int launch_encoding_backward(const EncArgs& a, int grad_dtype, cudaStream_t st);
 int launch_bins(const float* sorted, int64_t N, int64_t F, int n_q, float* edges, float* inv_w, int32_t* n_bins,

@@ -22,6 +22,15 @@ __device__ __forceinline__ f2_t pack2(float lo, float hi) {
 __device__ __forceinline__ void unpack2(f2_t v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
+// The two 32-bit halves of a packed pair as raw bits, and back.
+__device__ __forceinline__ void bits2(f2_t v, uint32_t& lo, uint32_t& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2_t from_bits2(uint32_t lo, uint32_t hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
 __device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
   f2_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));

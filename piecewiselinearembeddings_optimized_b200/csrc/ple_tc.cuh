@@ -1,0 +1,118 @@
+// ple_tc.cuh - 5th-generation tensor core (tcgen05) primitives for sm_100a,
+// written as inline PTX: shared-memory matrix descriptors (no swizzle), the
+// kind::f16 MMA with bf16 operands and an fp32 accumulator in tensor memory
+// (TMEM), commit to an mbarrier, iteration-limited mbarrier waits, TMEM
+// allocation and 32-lane loads.
+//
+// Canonical no-swizzle layouts (16-byte core-matrix rows, 8 rows per core
+// matrix, 128 bytes):
+//   K-major operand  (rows x K):  element (row, k) at core matrix
+//       (row / 8, k / 8), inside it row % 8 selects the 16-byte line and
+//       k % 8 the element.  LBO = byte step between k-blocks, SBO = byte step
+//       between row-blocks.
+//   MN-major operand (K x cols): element (k, col) at core matrix
+//       (col / 8, k / 8), inside it k % 8 selects the line and col % 8 the
+//       element.  LBO = byte step between k-blocks, SBO = byte step between
+//       col-blocks.
+// The accumulator of an M = 128 MMA occupies TMEM lanes 0..127 (row m in lane
+// m) and N consecutive 32-bit columns.
+#pragma once
+
+#include <stdint.h>
+
+namespace ple {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Shared-memory matrix descriptor: start address, LBO and SBO in 16-byte units,
+// descriptor version 1 (bit 46), base offset 0, layout type 0 (no swizzle).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | ((uint64_t)1 << 46);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), bf16 A
+// and B (bits 7-9, 10-12 = 1), A K-major (bit 15 = 0), B MN-major (bit 16 = 1),
+// N / 8 in bits 17-22, M / 16 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_bf16_a_k_b_mn(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (TMEM) = A * B (+ D when accumulate != 0); issued by one thread.
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the mbarrier once every tcgen05 operation this thread issued before has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Wait until the phase of the given parity has completed; false after `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int limit) {
+  const uint32_t a = smem_addr(bar);
+  for (int i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Generic-proxy shared-memory writes become visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Warp-wide: allocate ncols TMEM columns (power of two >= 32), address written to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Warp-wide: 8 consecutive 32-bit columns of this warp's 32 lanes (lane i of the
+// warp gets TMEM lane base + i).  Complete with wait_ld() before use.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Orders the uses of loaded registers after wait_ld(): volatile asm statements keep
+// their relative order, and this one redefines the registers.
+__device__ __forceinline__ void hold8(uint32_t (&r)[8]) {
+  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]));
+}
+
+// Warp-wide: store 8 consecutive 32-bit columns of this warp's 32 lanes; complete with wait_st().
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace ple
