@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--consumer", type=int, default=None, metavar="H",
+                    help="time the module fused into a following Linear(F*D -> H) (forward, bf16 autocast "
+                         "semantics) against the unfused embeddings kernel + cuBLAS, one GPU")
     return ap.parse_args()
 
 
@@ -163,6 +166,98 @@ def reference_arm(args, ws, rank):
     return 0
 
 
+def consumer_bench(args) -> int:
+    """The embeddings fused into the consumer's first Linear(F * D -> H): one step = one forward
+    (rtdl_num_embeddings_cuda::embeddings_linear_forward through the C ABI, bf16 autocast semantics,
+    bf16 output) over the configuration's batch; the same step unfused (the module's own fused kernel
+    writing [N, F, D] bf16, then cuBLAS addmm) is timed beside it.  Roofline: tensor (2 N F D H flop
+    per launch against the measured bf16 GEMM peak)."""
+    import torch
+
+    import rtdl_num_embeddings_cuda  # noqa: F401
+    from piecewiselinearembeddings_optimized_b200 import _native, workloads
+    from piecewiselinearembeddings_optimized_b200.module import pad_bin_tables
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    name, H = args.config, int(args.consumer)
+    n0, F, D, version, relu, _mode, _out = workloads.SPECS[name]
+    N = args.batch or min(n0, 131072)
+    wl = workloads.make_workload(name, n=8)
+    B = wl.max_n_bins
+    edges, inv_w, n_bins = [t.to(dev) for t in pad_bin_tables([torch.from_numpy(b) for b in wl.bins])]
+    W = torch.from_numpy(wl.weight).to(dev)
+    t = lambda a: None if a is None else torch.from_numpy(a).to(dev)  # noqa: E731
+    bias, w0, b0 = t(wl.bias), t(wl.w0), t(wl.b0)
+    epi = 2 if version == "B" else 1
+    gen = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(N, F, device=dev, generator=gen)
+    w1 = (torch.randn(H, F * D, device=dev, generator=gen) / (F * D) ** 0.5).to(torch.bfloat16)
+    b1 = torch.randn(H, device=dev, generator=gen) * 0.1
+    z = torch.empty(N, H, device=dev, dtype=torch.bfloat16)
+    lib = _native.capi()
+    ws_bytes = lib.ple_embeddings_linear_workspace_size(F, B, D, H, _native.DTYPE_BF16)
+    if ws_bytes == 0:
+        print(json.dumps({"error": "unsupported consumer shape"}))
+        return 1
+    wsp = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
+    wsa = (wsp.data_ptr() + 255) // 256 * 256
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    P = lambda a: None if a is None else a.data_ptr()  # noqa: E731
+    ops = torch.ops.rtdl_num_embeddings_cuda
+    b1h = b1.to(torch.bfloat16)
+
+    def fused():
+        _native.check(lib.ple_embeddings_linear_forward(
+            x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(), W.data_ptr(), P(bias), P(w0),
+            P(b0), epi, int(relu), _native.DTYPE_BF16, N, F, B, D, w1.data_ptr(), _native.DTYPE_BF16,
+            b1.data_ptr(), H, _native.DTYPE_BF16, z.data_ptr(), wsa, ws_bytes, sp), "embeddings_linear_forward")
+
+    def unfused():
+        e = ops.embeddings_forward(x, edges, inv_w, n_bins, W, bias, w0, b0, epi, relu, torch.bfloat16,
+                                   torch.bfloat16)
+        torch.addmm(b1h, e.view(N, -1), w1.t(), out=z)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in ev:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize(dev)
+        return float(np.median([a.elapsed_time(b) for a, b in ev]))
+
+    clocks = ClockSampler(gpu_id(torch, dev, 0))
+    clocks.start()
+    time.sleep(0.05)
+    t_fused = timed(fused)
+    t_unfused = timed(unfused)
+    clock_info = clocks.stop()
+    status = lib.ple_linear_status()
+    flop = 2.0 * N * F * D * H
+    peak = None
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        peak = float(json.loads(p.read_text()).get("bf16_tflops", 0)) or None
+    achieved = flop / (t_fused * 1e-3) / 1e12
+    line = {
+        "metric": f"PLE + Linear(F*D -> {H}) forward feature-embeddings/s (fused consumer)",
+        "value": N * F / (t_fused * 1e-3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_fused, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{name} shapes (N={N}, F={F}, B={B}, D={D}) -> Linear({F * D}, {H})",
+                   "inputs": "x [N, F] fp32 and the bf16 linear weight resident in HBM"},
+        "unfused_ms_per_step": t_unfused, "speedup_vs_unfused": t_unfused / t_fused,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if peak else None, "peak_source": "measured" if peak else None},
+        "status_word": status, "clocks": clock_info,
+    }
+    print(json.dumps(line))
+    return 0 if status == 0 else 1
+
+
 def config_block(name, n_global, ws):
     from piecewiselinearembeddings_optimized_b200 import workloads
 
@@ -178,6 +273,8 @@ def main() -> int:
     ws, rank, local = dist_env()
     if args.impl == "reference":
         return reference_arm(args, ws, rank)
+    if args.consumer:
+        return consumer_bench(args)
 
     import torch
     import torch.distributed as dist

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 4
+#define PLE_ABI_VERSION 5
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -264,6 +264,44 @@ int ple_encoding_backward(const void* grad_output, int grad_dtype, const float* 
  */
 int ple_compute_bins(const float* sorted_columns, int64_t n_rows, int64_t n_features, int n_bins,
                      float* bin_edges, float* inv_bin_widths, int32_t* n_bins_out, void* stream);
+
+/*
+ * Embeddings forward fused into the first Linear layer of its consumer
+ * (flatten + nn.Linear(F * D, H), the layer that follows the module in an
+ * MLP); the reference ends at the module output (module.py:207-248) and has
+ * no counterpart.
+ *   z[N, H] = flatten(y)[N, F * D] @ linear_weight[H, F * D]^T + linear_bias
+ * where y is ple_embeddings_forward's result in compute_dtype (BF16 = the
+ * autocast module output, rounded to bf16; F32 = the fp32 module output,
+ * rounded to bf16 for the product).  The product runs on the tensor cores
+ * with bf16 operands and fp32 accumulation, as an autocast nn.Linear does;
+ * y is never written to memory.
+ *   linear_weight  [H, F * D] BF16 (linear_weight_dtype = PLE_DTYPE_BF16)
+ *   linear_bias    [H] f32, may be NULL
+ *   output         [N, H] F32 or BF16, 16-byte aligned
+ *   d_embedding a multiple of 8; compute_dtype F32 or BF16.
+ * The workspace (256-byte aligned, ple_embeddings_linear_workspace_size bytes)
+ * receives per-call images of the tables and of linear_weight.
+ */
+size_t ple_embeddings_linear_workspace_size(int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                                            int64_t out_features, int compute_dtype); /* 0: unsupported */
+
+int ple_embeddings_linear_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                                  const int32_t* n_bins, const float* weight, const float* bias,
+                                  const float* w0, const float* b0, int epilogue, int activation,
+                                  int compute_dtype, int64_t batch, int64_t n_features,
+                                  int64_t max_n_bins, int64_t d_embedding, const void* linear_weight,
+                                  int linear_weight_dtype, const float* linear_bias,
+                                  int64_t out_features, int output_dtype, void* output,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Status word of ple_embeddings_linear_forward on the current device, as
+ * ple_tensor_core_status: 1 if a wait of the kernel ran past its iteration
+ * limit since the last call (that launch's output is incomplete), 0 if not,
+ * -1 if unreadable.  Reading clears it.
+ */
+int ple_linear_status(void);
 
 #ifdef __cplusplus
 }

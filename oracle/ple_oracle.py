@@ -278,6 +278,32 @@ def embeddings_forward(x, edges, inv_w, n_bins, W, *, version="A", activation=Fa
     return quantize(y, out_mode), z, k
 
 
+def embeddings_linear_forward(x, edges, inv_w, n_bins, W, W1, b1=None, *, version="A", activation=False,
+                              bias=None, w0=None, b0=None, mode="bf16", out_mode="f32"):
+    """The module output fed to ``flatten`` + ``nn.Linear(F * D, H)`` under bf16
+    autocast (the consumer step after ``module.py:207-248``; the reference has no
+    fused counterpart).
+
+    The Linear sees the module output rounded to bf16 (``mode`` "bf16": the
+    autocast module output; "f32": the fp32 output, rounded for the product) and
+    its weight rounded to bf16; the product is accumulated exactly here (float64)
+    and rounded to ``out_mode``.  Returns ``(z, e, scale)``: the output ``[N, H]``,
+    the bf16 embeddings ``[N, F, D]`` and ``|e| @ |W1|^T`` (the magnitude that
+    bounds the rounding error of each output, for tolerances).
+    """
+    e, _, _ = embeddings_forward(x, edges, inv_w, n_bins, W, version=version, activation=activation,
+                                 bias=bias, w0=w0, b0=b0, mode=mode, out_mode="bf16")
+    n = e.shape[0]
+    e2 = e.reshape(n, -1).astype(np.float64)
+    w = bf16_round(np.asarray(W1, np.float32)).astype(np.float64)
+    z = e2 @ w.T
+    if b1 is not None:
+        z = z + np.asarray(b1, np.float64)[None]
+    with np.errstate(invalid="ignore"):
+        scale = np.abs(e2) @ np.abs(w).T
+    return quantize(z.astype(np.float32), out_mode), e, scale
+
+
 def embeddings_backward(g, x, edges, inv_w, n_bins, W, *, version="A", activation=False,
                         bias=None, w0=None, b0=None, mode="f32"):
     """Autograd of ``embeddings_forward``.

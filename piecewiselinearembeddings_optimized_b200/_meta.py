@@ -133,3 +133,17 @@ def _compute_bins_fake(x, n_bins: int):
     return (torch.empty((f, n_bins + 1), dtype=torch.float32, device=x.device),
             torch.empty((f, n_bins), dtype=torch.float32, device=x.device),
             torch.empty((f,), dtype=torch.int32, device=x.device))
+
+
+@torch.library.register_fake("rtdl_num_embeddings_cuda::embeddings_linear_forward")
+def _embeddings_linear_forward_fake(x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, epilogue: int,
+                                    activation: bool, compute_dtype: torch.dtype, linear_weight, linear_bias,
+                                    output_dtype: torch.dtype):
+    _check_tables(x, bin_edges, inv_bin_widths, n_bins, weight)
+    torch._check(linear_weight.ndim == 2, lambda: "linear_weight must have shape [H, F * D]")
+    torch._check(linear_weight.shape[1] == weight.shape[0] * weight.shape[2],
+                 lambda: "linear_weight.shape[1] must equal n_features * d_embedding")
+    torch._check(linear_weight.dtype == torch.bfloat16, lambda: "linear_weight must be bfloat16")
+    torch._check(output_dtype in (torch.float32, torch.bfloat16), lambda: "output_dtype must be float32 or bfloat16")
+    torch._check(compute_dtype in (torch.float32, torch.bfloat16), lambda: "compute_dtype must be float32 or bfloat16")
+    return torch.empty((x.shape[0], linear_weight.shape[0]), dtype=output_dtype, device=x.device)

@@ -79,6 +79,13 @@ def capi() -> ctypes.CDLL:
     lib.ple_encoding_forward.argtypes = [P, P, P, P, P, I, I64, I64, I64, I64, I, P, P]
     lib.ple_encoding_backward.restype = I
     lib.ple_encoding_backward.argtypes = [P, I, P, P, P, P, P, I, I64, I64, I64, I64, P, P]
+    lib.ple_linear_status.restype = I
+    lib.ple_linear_status.argtypes = []
+    lib.ple_embeddings_linear_workspace_size.restype = SZ
+    lib.ple_embeddings_linear_workspace_size.argtypes = [I64, I64, I64, I64, I]
+    lib.ple_embeddings_linear_forward.restype = I
+    lib.ple_embeddings_linear_forward.argtypes = [P, P, P, P, P, P, P, P, I, I, I, I64, I64, I64, I64,
+                                                  P, I, P, I64, I, P, P, SZ, P]
     lib.ple_compute_bins.restype = I
     lib.ple_compute_bins.argtypes = [P, I64, I64, I, P, P, P, P]
     _capi = lib

@@ -12,6 +12,8 @@
 //   embeddings_forward / embeddings_backward.
 // Added (the standalone encoding, upstream PiecewiseLinearEncoding):
 //   encoding_forward / encoding_backward.
+// Added (the module fused into its consumer's first Linear layer):
+//   embeddings_linear_forward.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -243,6 +245,55 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
   return {gx, gw, gb, gw0, gb0};
 }
 
+at::Tensor ple_embeddings_linear_forward_op(const at::Tensor& x, const at::Tensor& bin_edges,
+                                            const at::Tensor& inv_bin_widths, const at::Tensor& n_bins,
+                                            const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+                                            const std::optional<at::Tensor>& w0,
+                                            const std::optional<at::Tensor>& b0, int64_t epilogue, bool activation,
+                                            at::ScalarType compute_dtype, const at::Tensor& linear_weight,
+                                            const std::optional<at::Tensor>& linear_bias,
+                                            at::ScalarType output_dtype) {
+  check_tables(x, bin_edges, inv_bin_widths, n_bins, weight);
+  check_param(bias, weight, "bias");
+  check_param(w0, weight, "w0");
+  check_param(b0, weight, "b0");
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  TORCH_CHECK(linear_weight.is_cuda() && linear_weight.device() == x.device(),
+              "linear_weight must be on x's CUDA device");
+  TORCH_CHECK(linear_weight.scalar_type() == at::kBFloat16, "linear_weight must be bfloat16");
+  TORCH_CHECK(linear_weight.dim() == 2 && linear_weight.size(1) == F * D,
+              "linear_weight must have shape [out_features, n_features * d_embedding]");
+  TORCH_CHECK(linear_weight.is_contiguous(), "linear_weight must be contiguous");
+  const int64_t H = linear_weight.size(0);
+  if (linear_bias.has_value()) {
+    TORCH_CHECK(linear_bias->is_cuda() && linear_bias->device() == x.device(), "linear_bias must be on x's device");
+    TORCH_CHECK(linear_bias->scalar_type() == at::kFloat, "linear_bias must be float32");
+    TORCH_CHECK(linear_bias->dim() == 1 && linear_bias->size(0) == H, "linear_bias must have shape [out_features]");
+    TORCH_CHECK(linear_bias->is_contiguous(), "linear_bias must be contiguous");
+  }
+  TORCH_CHECK(output_dtype == at::kFloat || output_dtype == at::kBFloat16,
+              "output_dtype must be float32 or bfloat16");
+  TORCH_CHECK(compute_dtype == at::kFloat || compute_dtype == at::kBFloat16,
+              "compute_dtype must be float32 or bfloat16");
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty({N, H}, x.options().dtype(output_dtype));
+  if (N == 0) return out;
+  const size_t need = ple_embeddings_linear_workspace_size(F, B, D, H, to_code(compute_dtype));
+  TORCH_CHECK(need > 0, "rtdl_num_embeddings_cuda::embeddings_linear_forward: unsupported shape (d_embedding must "
+              "be a multiple of 8)");
+  at::Tensor ws = at::empty({(int64_t)need + 256}, x.options().dtype(at::kByte));
+  void* wp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~(uintptr_t)255);
+  check_status(ple_embeddings_linear_forward(
+                   x.data_ptr<float>(), bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                   n_bins.data_ptr<int32_t>(), weight.data_ptr<float>(), ptr_or_null(bias), ptr_or_null(w0),
+                   ptr_or_null(b0), (int)epilogue, activation ? 1 : 0, to_code(compute_dtype), N, F, B, D,
+                   linear_weight.data_ptr(), PLE_DTYPE_BF16,
+                   linear_bias.has_value() ? linear_bias->data_ptr<float>() : nullptr, H, to_code(output_dtype),
+                   out.data_ptr(), wp, need, stream_of(x)),
+               "rtdl_num_embeddings_cuda::embeddings_linear_forward");
+  return out;
+}
+
 void check_encoding(const at::Tensor& x, const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
                     const at::Tensor& n_bins, const std::optional<at::Tensor>& col_offsets, int64_t layout,
                     int64_t total_bins) {
@@ -361,6 +412,10 @@ TORCH_LIBRARY(rtdl_num_embeddings_cuda, m) {
       "encoding_backward(Tensor grad_output, Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, "
       "Tensor? col_offsets, int layout, int total_bins) -> Tensor");
   m.def("compute_bins(Tensor x, int n_bins) -> (Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins)");
+  m.def(
+      "embeddings_linear_forward(Tensor x, Tensor bin_edges, Tensor inv_bin_widths, Tensor n_bins, Tensor weight, "
+      "Tensor? bias, Tensor? w0, Tensor? b0, int epilogue, bool activation, ScalarType compute_dtype, "
+      "Tensor linear_weight, Tensor? linear_bias, ScalarType output_dtype) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
@@ -371,4 +426,5 @@ TORCH_LIBRARY_IMPL(rtdl_num_embeddings_cuda, CUDA, m) {
   m.impl("encoding_forward", &ple_encoding_forward_op);
   m.impl("encoding_backward", &ple_encoding_backward_op);
   m.impl("compute_bins", &ple_compute_bins_op);
+  m.impl("embeddings_linear_forward", &ple_embeddings_linear_forward_op);
 }

@@ -133,6 +133,8 @@ int ple_abi_version(void) { return PLE_ABI_VERSION; }
 
 int ple_tensor_core_status(void) { return tensor_core_status(); }
 
+int ple_linear_status(void) { return linear_status(); }
+
 const char* ple_status_string(int status) {
   switch (status) {
     case PLE_OK: return "ok";
@@ -389,6 +391,52 @@ int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, con
                        epilogue, activation, compute_dtype, batch, n_features, max_n_bins, d_embedding, bin_indices,
                        bin_index_dtype, grad_x, grad_weight, grad_bias, grad_w0, grad_b0, scratch,
                        (size_t)PLE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+size_t ple_embeddings_linear_workspace_size(int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                                            int64_t out_features, int compute_dtype) {
+  if (n_features <= 0 || max_n_bins <= 0 || max_n_bins > 256 || d_embedding <= 0 || d_embedding > kMaxD ||
+      out_features <= 0 || n_features > ((int64_t)1 << 30))
+    return 0;
+  if (compute_dtype != PLE_DTYPE_F32 && compute_dtype != PLE_DTYPE_BF16) return 0;
+  return linear_workspace_bytes(n_features, max_n_bins, d_embedding, out_features, compute_dtype);
+}
+
+int ple_embeddings_linear_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
+                                  const int32_t* n_bins, const float* weight, const float* bias, const float* w0,
+                                  const float* b0, int epilogue, int activation, int compute_dtype, int64_t batch,
+                                  int64_t n_features, int64_t max_n_bins, int64_t d_embedding,
+                                  const void* linear_weight, int linear_weight_dtype, const float* linear_bias,
+                                  int64_t out_features, int output_dtype, void* output, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  g_msg[0] = 0;
+  int st = check_sizes(batch, n_features, max_n_bins, d_embedding);
+  if (st) return st;
+  if ((st = check_tables(bin_edges, inv_bin_widths, n_bins, weight))) return st;
+  if (epilogue != kEpiNone && epilogue != kEpiA && epilogue != kEpiB)
+    return set_error(PLE_ERR_INVALID_ARGUMENT, "bad epilogue");
+  if (epilogue == kEpiA && !bias) return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue A needs bias");
+  if (epilogue == kEpiB && (!w0 || !b0)) return set_error(PLE_ERR_INVALID_ARGUMENT, "epilogue B needs w0 and b0");
+  if (compute_dtype != PLE_DTYPE_F32 && compute_dtype != PLE_DTYPE_BF16)
+    return set_error(PLE_ERR_UNSUPPORTED, "embeddings-linear: compute dtype must be F32 or BF16");
+  if (linear_weight_dtype != PLE_DTYPE_BF16)
+    return set_error(PLE_ERR_UNSUPPORTED, "embeddings-linear: the linear weight must be BF16");
+  if (output_dtype != PLE_DTYPE_F32 && output_dtype != PLE_DTYPE_BF16)
+    return set_error(PLE_ERR_UNSUPPORTED, "embeddings-linear: output dtype must be F32 or BF16");
+  if (out_features <= 0) return set_error(PLE_ERR_SHAPE, "out_features must be positive");
+  if (out_features > ((int64_t)1 << 20)) return set_error(PLE_ERR_UNSUPPORTED, "out_features above 2^20");
+  if (batch > 0 && out_features > INT64_MAX / batch) return set_error(PLE_ERR_OVERFLOW, "N * out_features overflows");
+  if (!linear_weight) return set_error(PLE_ERR_INVALID_ARGUMENT, "linear_weight is required");
+  if (batch == 0) return PLE_OK;
+  if (!x || !output) return set_error(PLE_ERR_INVALID_ARGUMENT, "x and output are required");
+  if (!aligned(output, 16)) return set_error(PLE_ERR_ALIGNMENT, "output must be 16-byte aligned");
+  LinearCall c{};
+  c.x = x; c.edges = bin_edges; c.inv_w = inv_bin_widths; c.n_bins = n_bins; c.W = weight;
+  c.bias = bias; c.w0 = w0; c.b0 = b0; c.W1 = linear_weight; c.b1 = linear_bias; c.z = output;
+  c.ws = workspace; c.ws_bytes = workspace_bytes; c.N = batch; c.H = out_features;
+  c.F = (int)n_features; c.B = (int)max_n_bins; c.D = (int)d_embedding;
+  c.epi = epilogue; c.relu = activation ? 1 : 0; c.compute_dtype = compute_dtype; c.out_dtype = output_dtype;
+  return launch_linear(c, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -77,6 +77,26 @@ struct EncArgs {
   int F, B, layout;
 };
 
+// embeddings forward fused into a consumer Linear (ple_linear.cu)
+struct LinearCall {
+  const float* x;
+  const float* edges;
+  const float* inv_w;
+  const int32_t* n_bins;
+  const float* W;
+  const float* bias;
+  const float* w0;
+  const float* b0;
+  const void* W1;  // bf16 [H, F * D]
+  const float* b1;  // [H] or null
+  void* z;          // [N, H]
+  void* ws;
+  size_t ws_bytes;
+  int64_t N, H;
+  int F, B, D;
+  int epi, relu, compute_dtype, out_dtype;
+};
+
 // error plumbing (ple_capi.cu)
 int set_error(int code, const char* msg);
 int set_cuda_error(cudaError_t e, const char* what);
@@ -90,6 +110,9 @@ int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaS
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
 int tensor_core_status();
+int launch_linear(const LinearCall& c, cudaStream_t st);
+size_t linear_workspace_bytes(int64_t F, int64_t B, int64_t D, int64_t H, int compute_dtype);
+int linear_status();
 int launch_encoding_forward(const EncArgs& a, int output_dtype, cudaStream_t st);
 int launch_encoding_backward(const EncArgs& a, int grad_dtype, cudaStream_t st);
 int launch_bins(const float* sorted, int64_t N, int64_t F, int n_q, float* edges, float* inv_w, int32_t* n_bins,

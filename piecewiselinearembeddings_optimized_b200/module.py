@@ -146,6 +146,69 @@ class CudaPiecewiseLinearEmbeddings(Base):
         )
 
 
+class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
+    """``linear(embeddings(x).flatten(1))`` with the embeddings fused into the Linear.
+
+    Wraps an existing ``CudaPiecewiseLinearEmbeddings`` and the
+    ``nn.Linear(F * D, H)`` that consumes its flattened output (parameters are
+    shared, not copied), so it replaces ``nn.Sequential(embeddings,
+    nn.Flatten(), linear)`` in an MLP.  On CUDA under bf16 autocast the three
+    run as one tensor-core kernel (``rtdl_num_embeddings_cuda::
+    embeddings_linear_forward``) whose ``[N, F, D]`` intermediate never reaches
+    memory; the result is bf16, as autocast's Linear returns.  With
+    ``bf16_linear=True`` and no autocast the fp32 module output is rounded to
+    bf16 for the product and the result is fp32.  Everything else (CPU inputs,
+    fp16 autocast, plain fp32, d_embedding not a multiple of 8) runs the
+    composition: the module's own kernel followed by ``linear``.
+    """
+
+    def __init__(self, embeddings: CudaPiecewiseLinearEmbeddings, linear: torch.nn.Linear, *,
+                 bf16_linear: bool = False) -> None:
+        super().__init__()
+        d_in = embeddings.n_features * embeddings.d_embedding
+        if linear.in_features != d_in:
+            raise ValueError(f"linear.in_features must be n_features * d_embedding = {d_in}, "
+                             f"got {linear.in_features}")
+        self.embeddings = embeddings
+        self.linear = linear
+        self.bf16_linear = bf16_linear
+
+    def _fused_dtypes(self, x: Tensor):
+        if x.device.type != "cuda" or self.embeddings.d_embedding % 8 != 0:
+            return None
+        if torch.is_autocast_enabled("cuda"):
+            if torch.get_autocast_dtype("cuda") != torch.bfloat16:
+                return None
+            return torch.bfloat16, torch.bfloat16
+        return (torch.float32, torch.float32) if self.bf16_linear else None
+
+    def forward(self, x: Tensor) -> Tensor:
+        dtypes = self._fused_dtypes(x)
+        if dtypes is None:
+            return self.linear(self.embeddings(x).flatten(1))
+        emb = self.embeddings
+        if x.ndim != 2 or x.shape[1] != emb.n_features:
+            raise ValueError(f"Expected x of shape [batch_size, {emb.n_features}]")
+        if x.device != emb._cuda_bin_edges.device:
+            raise RuntimeError("x and the module must be on the same CUDA device")
+        emb._check_cuda_inputs(x)
+        compute, out_dtype = dtypes
+        if emb.linear0 is not None:
+            epilogue, bias, w0, b0 = EPILOGUE_B, None, emb.linear0.weight, emb.linear0.bias
+        elif emb.linear.bias is not None:
+            epilogue, bias, w0, b0 = EPILOGUE_A, emb.linear.bias, None, None
+        else:
+            epilogue, bias, w0, b0 = EPILOGUE_NONE, None, None, None
+        w1 = self.linear.weight.to(torch.bfloat16).contiguous()
+        b1 = self.linear.bias
+        if b1 is not None and compute == torch.bfloat16:
+            b1 = b1.to(torch.bfloat16).float()  # autocast's Linear adds a bf16 bias
+        return torch.ops.rtdl_num_embeddings_cuda.embeddings_linear_forward(
+            x, emb._cuda_bin_edges, emb._cuda_inv_bin_widths, emb._cuda_n_bins, emb.linear.weight,
+            bias, w0, b0, epilogue, emb.activation is not None, compute, w1, b1, out_dtype,
+        )
+
+
 ENCODING_RAGGED, ENCODING_PADDED = 0, 1
 
 

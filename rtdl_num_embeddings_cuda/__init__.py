@@ -13,11 +13,13 @@ from piecewiselinearembeddings_optimized_b200 import _meta as _meta  # noqa: E40
 from piecewiselinearembeddings_optimized_b200 import _autograd as _autograd  # noqa: E402,F401
 from piecewiselinearembeddings_optimized_b200.module import (  # noqa: E402
     CudaPiecewiseLinearEmbeddings,
+    CudaPiecewiseLinearEmbeddingsLinear,
     CudaPiecewiseLinearEncoding,
 )
 
 from piecewiselinearembeddings_optimized_b200.bins import bin_tables, compute_bins  # noqa: E402
 
-__all__ = ["CudaPiecewiseLinearEmbeddings", "CudaPiecewiseLinearEncoding", "compute_bins", "bin_tables"]
+__all__ = ["CudaPiecewiseLinearEmbeddings", "CudaPiecewiseLinearEmbeddingsLinear", "CudaPiecewiseLinearEncoding",
+           "compute_bins", "bin_tables"]
 
 __version__ = "0.2.0.dev0+b200"
