@@ -74,6 +74,8 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
   int pow2 = 1;
   while (pow2 < a.B + 1) pow2 <<= 1;
   a.pow2 = pow2;
+  a.lgk = 0;
+  while ((1 << a.lgk) < a.B) ++a.lgk;
   const size_t optin = device_max_smem_optin();
   constexpr int kWarps = kBwdThreads / 32;
   int lgWarps = 0;
@@ -88,7 +90,7 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
     for (int lgSt = 12; lgSt >= 7; --lgSt) {
       if (lgSt < lgWf) break;
       BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G, nc};
-      const size_t bytes = bwd_layout_bytes(a.B, a.D, pow2, m, nullptr, nullptr);
+      const size_t bytes = bwd_layout_bytes(a.B, a.D, 1 << a.lgk, m, nullptr, nullptr);
       if (bytes > optin) continue;
       const int score = lgFc + lgSt;
       if (score > best) {

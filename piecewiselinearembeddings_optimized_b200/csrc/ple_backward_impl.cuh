@@ -75,7 +75,8 @@ __host__ __device__ __forceinline__ int table_stride(int Fc, int D) {
 
 struct BwdLayout {
   float *sT, *sS, *sH, *sU;  // [B][ts] rows, feature i at i * D (bin-major, padded)
-  float *sE, *sR;            // [pow2][Fc] edges, [B][Fc] inverse widths
+  float *sK, *sE, *sR;       // [2^lgk][Fc] search keys (interior edges), [B][Fc] left edges e_k,
+                             // [B][Fc] inverse widths
   float *sX;                 // [2][S_t][Fc] x tiles
   float *sGX;                // [Fc][S_t][nc] grad_x shares
   float *sCarry;             // [Fc][G][2][D]
@@ -84,7 +85,7 @@ struct BwdLayout {
   int *sN, *sCnt, *sCarryBin, *sTie;  // sTie[Fc]: the tile has an edge tie in feature i
 };
 
-__host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int pow2, const BwdDims& m,
+__host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int key_rows, const BwdDims& m,
                                                             BwdLayout* L, unsigned char* base) {
   const size_t tab = (size_t)B * table_stride(m.Fc, D);
   size_t off = 0;
@@ -98,7 +99,8 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int po
   unsigned char* pGX = take((size_t)m.Fc * m.S_t * m.nc * 4);
   unsigned char* pEnt = take((size_t)m.Fc * (m.S_t + m.G) * 8);
   unsigned char* pX = take((size_t)2 * m.S_t * m.Fc * 4);
-  unsigned char* pE = take((size_t)pow2 * m.Fc * 4);
+  unsigned char* pK = take((size_t)key_rows * m.Fc * 4);
+  unsigned char* pE = take((size_t)B * m.Fc * 4);
   unsigned char* pR = take((size_t)B * m.Fc * 4);
   unsigned char* pN = take((size_t)m.Fc * 4);
   unsigned char* pCnt = take((size_t)m.Fc * B * m.Wf * 4);
@@ -114,6 +116,7 @@ __host__ __device__ __forceinline__ size_t bwd_layout_bytes(int B, int D, int po
     L->sGX = reinterpret_cast<float*>(pGX);
     L->sEnt = reinterpret_cast<float2*>(pEnt);
     L->sX = reinterpret_cast<float*>(pX);
+    L->sK = reinterpret_cast<float*>(pK);
     L->sE = reinterpret_cast<float*>(pE);
     L->sR = reinterpret_cast<float*>(pR);
     L->sN = reinterpret_cast<int*>(pN);
@@ -452,10 +455,24 @@ __device__ __forceinline__ void walk_block(const WalkCtx& w, WalkIn<GT, VEC> (&i
 // The chunk's tables for one segment: edges (transposed for the search),
 // inverse widths, S = q(W) in logical bin order and its exclusive prefix T;
 // H/U zeroed.
+// Four interleaved key counts (key_count over the transposed key table [2^LG][Fc], column ii[j]).
+template <int LG>
+__device__ __forceinline__ void key_count4(const float (&xs)[4], int (&c)[4], const float* sK, const int (&ii)[4],
+                                           int lgFc) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) c[j] = 0;
+#pragma unroll
+  for (int h = (1 << LG) >> 1; h > 0; h >>= 1) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (!(xs[j] < sK[((c[j] + h - 1) << lgFc) + ii[j]])) c[j] += h;
+  }
+}
+
 template <typename QT>
 __device__ __forceinline__ void stage_tables(const BwdArgs& a, const BwdLayout& L, int f0, int fc, int lgFc, int ts,
                                              int tid, int nthr) {
-  const int Fc = 1 << lgFc, B = a.B, D = a.D, pow2 = a.pow2;
+  const int Fc = 1 << lgFc, B = a.B, D = a.D, nkeys = 1 << a.lgk;
   for (int i = tid; i < Fc; i += nthr) {
     int n = i < fc ? a.n_bins[f0 + i] : 1;
     L.sN[i] = n < 1 ? 1 : (n > B ? B : n);
@@ -466,11 +483,16 @@ __device__ __forceinline__ void stage_tables(const BwdArgs& a, const BwdLayout& 
     L.sS[idx] = 0.0f;
   }
   __syncthreads();
-  for (int idx = tid; idx < pow2 * Fc; idx += nthr) {
+  // search keys: interior edges e_1 .. e_{n-1}, then +inf (key_count capped at n - 1 = the clamped bin)
+  for (int idx = tid; idx < nkeys * Fc; idx += nthr) {
     const int j = idx >> lgFc, i = idx & (Fc - 1);
     float e = __int_as_float(0x7f800000);
-    if (i < fc && j <= L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j];
-    L.sE[idx] = e;
+    if (i < fc && j + 1 < L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j + 1];
+    L.sK[idx] = e;
+  }
+  for (int idx = tid; idx < B * Fc; idx += nthr) {  // left edges e_k of the real bins
+    const int j = idx >> lgFc, i = idx & (Fc - 1);
+    L.sE[idx] = (i < fc && j < L.sN[i]) ? a.edges[(int64_t)(f0 + i) * (B + 1) + j] : 0.0f;
   }
   for (int idx = tid; idx < B * Fc; idx += nthr) {
     const int j = idx >> lgFc, i = idx & (Fc - 1);
@@ -515,7 +537,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
   const int ES = S_t + G;  // entries per feature (segment-major, see phase C)
   const int ts = table_stride(Fc, D);
   BwdLayout L;
-  bwd_layout_bytes(B, D, a.pow2, BwdDims{Fc, Wf, S_t, G, nc}, &L, smem_raw);
+  bwd_layout_bytes(B, D, 1 << a.lgk, BwdDims{Fc, Wf, S_t, G, nc}, &L, smem_raw);
 
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int lane = tid & 31, wid = tid >> 5;
@@ -631,23 +653,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
               }
             }
           } else {
-            // count of edges <= x over the padded pow2 table (as edge_count), four searches interleaved
+            // count of interior edges <= x (capped at n - 1: the clamped bin), four searches interleaved
             float xs[4];
-            int base[4];
+            int cnt[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) xs[j] = ok[j] ? sX[p0 + j * nthr] : 0.f;
+            switch (a.lgk) {
+#define PLE_BWD_COUNT(LL) \
+  case LL: key_count4<LL>(xs, cnt, L.sK, ii, lgFc); break;
+              PLE_BWD_COUNT(0) PLE_BWD_COUNT(1) PLE_BWD_COUNT(2) PLE_BWD_COUNT(3) PLE_BWD_COUNT(4)
+              PLE_BWD_COUNT(5) PLE_BWD_COUNT(6) PLE_BWD_COUNT(7) PLE_BWD_COUNT(8)
+#undef PLE_BWD_COUNT
+              default:
+#pragma unroll
+                for (int j = 0; j < 4; ++j) cnt[j] = 0;
+                break;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              xs[j] = ok[j] ? sX[p0 + j * nthr] : 0.f;
-              base[j] = 0;
-            }
-            for (int half = a.pow2 >> 1; half > 0; half >>= 1) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                if (!(xs[j] < L.sE[((base[j] + half - 1) << lgFc) + ii[j]])) base[j] += half;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (!(xs[j] < L.sE[(base[j] << lgFc) + ii[j]])) base[j] += 1;
-              kk[j] = logical_bin(base[j], L.sN[ii[j]]);
+              const int n1 = L.sN[ii[j]] - 1;
+              kk[j] = cnt[j] < n1 ? cnt[j] : n1;
             }
           }
 #pragma unroll

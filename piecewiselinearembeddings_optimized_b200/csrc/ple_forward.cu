@@ -3,14 +3,15 @@
 // The grid is persistent (SMs x resident CTAs); CTA j owns an equal contiguous
 // range of the flattened (feature chunk, sample) space - one or a few
 // (chunk of Fc consecutive features, sample range) segments.  Per segment it
-// stages the chunk's edges (+inf-padded rows), inverse widths and two tables
-// in shared memory, laid out bin-major [k][feature][d]:
+// stages the chunk's search keys (interior edges e_1 .. e_{n-1}, +inf padded
+// to 2^L - 1), {e_k, r_k} pairs and two tables in shared memory, the tables
+// laid out bin-major [k][feature][d]:
 //     T[k][i][:] = sum_{j<k} q(W[i, j, :])          (prefix of full bins)
 //     S[k][i][:] = q(W[i, phys(k), :])              (slope of the active bin)
 // so that x_ple = q(fma(q(t), S[k], T[k])) (reference forward_cuda.cu:135-176,
 // 258-273).  Then, per tile of samples:
 //   x tile   [S_t][Fc] arrives by cp.async, double-buffered one tile ahead;
-//   phase 1  one thread per (sample, feature): bin search, {k, q(t), x} -> smem
+//   phase 1  one thread per (sample, feature): L-probe bin search, {k, q(t), x} -> smem
 //            (+ bin-index store for the reference op);
 //   phase 2  one thread per VEC-wide chunk of an output row, each thread on a
 //            fixed column (its epilogue parameters live in registers): one
@@ -41,7 +42,8 @@ __device__ __forceinline__ void store_out(OT* p, const FV<VEC>& y) {
 
 // Shared-memory layout of one CTA (sizes from FwdArgs).
 struct FwdLayout {
-  float *sT, *sS, *sXb, *sE, *sR;
+  float *sT, *sS, *sXb, *sK;
+  float2* sL;
   float4* sQ;
   int* sN;
 };
@@ -58,27 +60,55 @@ __host__ __device__ __forceinline__ size_t fwd_layout(const FwdArgs& a, FwdLayou
   unsigned char* pT = take(2 * tab * 4);
   unsigned char* pQ = take((size_t)a.S_t * Fc * 16);
   unsigned char* pX = take((size_t)2 * a.S_t * Fc * 4);
-  unsigned char* pE = take((size_t)Fc * a.ldE * 4);
-  unsigned char* pR = take((size_t)Fc * a.B * 4);
+  unsigned char* pE = take((size_t)Fc * a.ldK * 4);
+  unsigned char* pR = take((size_t)Fc * a.B * 8);
   unsigned char* pN = take((size_t)Fc * 4);
   if (L) {
     L->sT = reinterpret_cast<float*>(pT);
     L->sS = L->sT + tab;
     L->sQ = reinterpret_cast<float4*>(pQ);
     L->sXb = reinterpret_cast<float*>(pX);
-    L->sE = reinterpret_cast<float*>(pE);
-    L->sR = reinterpret_cast<float*>(pR);
+    L->sK = reinterpret_cast<float*>(pE);
+    L->sL = reinterpret_cast<float2*>(pR);
     L->sN = reinterpret_cast<int*>(pN);
   }
   return off;
 }
 
+// Phase 1 of a tile: per (sample, feature) the bin (L-probe search over the
+// feature's interior edges), the position and the record {k * kstride, q(t), x}.
+template <int L, typename QT>
+__device__ __forceinline__ void fwd_phase1(const FwdArgs& a, const FwdLayout& Ly, const float* sX, int ns, int fc,
+                                           int kstride, int64_t t0, int f0, int tid, int nthr) {
+  const int lgFc = a.lgFc, Fc = 1 << lgFc, ldK = a.ldK, B = a.B;
+  for (int p = tid; p < (ns << lgFc); p += nthr) {
+    const int i = p & (Fc - 1);
+    const float xv = sX[p];
+    float4 q = make_float4(0.0f, 0.0f, xv, 0.0f);
+    if (i < fc) {
+      const int c = key_count<L>(xv, Ly.sK + i * ldK);
+      const int n1 = Ly.sN[i] - 1;
+      const int k = c < n1 ? c : n1;
+      const float2 er = Ly.sL[i * B + k];
+      q.x = __int_as_float(k * kstride);
+      q.y = quantize<QT>((xv - er.x) * er.y);
+      if (a.bin_idx != nullptr) {
+        const int64_t pair = (t0 + (p >> lgFc)) * a.F + f0 + i;
+        if (a.bin_idx_bytes == 1) reinterpret_cast<uint8_t*>(a.bin_idx)[pair] = (uint8_t)k;
+        else if (a.bin_idx_bytes == 2) reinterpret_cast<int16_t*>(a.bin_idx)[pair] = (int16_t)k;
+        else reinterpret_cast<int32_t*>(a.bin_idx)[pair] = k;
+      }
+    }
+    Ly.sQ[p] = q;
+  }
+}
+
 template <typename QT, typename OT, int VEC, int EPI, bool RELU>
-__global__ void __launch_bounds__(kFwdMaxThreads)
+__global__ void __launch_bounds__(kFwdMaxThreads, 2)
 ple_fwd_kernel(const FwdArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lgFc = a.lgFc;
-  const int Fc = 1 << lgFc, B = a.B, D = a.D, pow2 = a.pow2, S_t = a.S_t, ldE = a.ldE;
+  const int Fc = 1 << lgFc, B = a.B, D = a.D, S_t = a.S_t, ldK = a.ldK;
   const int nc = D / VEC;
   const int R = Fc * nc;
   FwdLayout L;
@@ -133,15 +163,18 @@ ple_fwd_kernel(const FwdArgs a) {
       L.sN[i] = n < 1 ? 1 : (n > B ? B : n);
     }
     __syncthreads();
-    for (int idx = tid; idx < Fc * ldE; idx += nthr) {  // feature-major edge rows, +inf padded
-      const int i = idx / ldE, j = idx - i * ldE;
+    for (int idx = tid; idx < Fc * ldK; idx += nthr) {  // feature-major key rows: e_1 .. e_{n-1}, +inf
+      const int i = idx / ldK, j = idx - i * ldK;
       float e = __int_as_float(0x7f800000);
-      if (i < fc && j <= L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j];
-      L.sE[idx] = e;
+      if (i < fc && j + 1 < L.sN[i]) e = a.edges[(int64_t)(f0 + i) * (B + 1) + j + 1];
+      L.sK[idx] = e;
     }
-    for (int idx = tid; idx < Fc * B; idx += nthr) {
+    for (int idx = tid; idx < Fc * B; idx += nthr) {  // {e_k, r_k}
       const int i = idx / B, j = idx - i * B;
-      L.sR[idx] = (i < fc && j < L.sN[i]) ? a.inv_w[(int64_t)(f0 + i) * B + j] : 0.0f;
+      float2 v = make_float2(0.0f, 0.0f);
+      if (i < fc && j < L.sN[i])
+        v = make_float2(a.edges[(int64_t)(f0 + i) * (B + 1) + j], a.inv_w[(int64_t)(f0 + i) * B + j]);
+      L.sL[idx] = v;
     }
     const float* Wc = a.W + (int64_t)f0 * B * D;
     for (int idx = tid; idx < fc * B * D; idx += nthr) {
@@ -186,24 +219,13 @@ ple_fwd_kernel(const FwdArgs a) {
       __syncthreads();  // x tile visible; previous phase 2 done with sQ and the other buffer
       if (t0 + S_t < s_end) load_x(t0 + S_t, (int)min64(S_t, s_end - t0 - S_t), L.sXb + (buf ^ 1) * S_t * Fc);
       // ---- phase 1: bins, positions -> sQ[s][i] = {k, q(t), x}
-      for (int p = tid; p < (ns << lgFc); p += nthr) {
-        const int i = p & (Fc - 1);
-        const float xv = sX[p];
-        float4 q = make_float4(0.0f, 0.0f, xv, 0.0f);
-        if (i < fc) {
-          const float* row = L.sE + i * ldE;
-          const int k = logical_bin(edge_count_row(xv, row, pow2), L.sN[i]);
-          const float t = (xv - row[k]) * L.sR[i * B + k];
-          q.x = __int_as_float(k * kstride);
-          q.y = quantize<QT>(t);
-          if (a.bin_idx != nullptr) {
-            const int64_t pair = (t0 + (p >> lgFc)) * a.F + f0 + i;
-            if (a.bin_idx_bytes == 1) reinterpret_cast<uint8_t*>(a.bin_idx)[pair] = (uint8_t)k;
-            else if (a.bin_idx_bytes == 2) reinterpret_cast<int16_t*>(a.bin_idx)[pair] = (int16_t)k;
-            else reinterpret_cast<int32_t*>(a.bin_idx)[pair] = k;
-          }
-        }
-        L.sQ[p] = q;
+      switch (a.lgk) {
+#define PLE_FWD_P1(LL) \
+  case LL: fwd_phase1<LL, QT>(a, L, sX, ns, fc, kstride, t0, f0, tid, nthr); break;
+        PLE_FWD_P1(0) PLE_FWD_P1(1) PLE_FWD_P1(2) PLE_FWD_P1(3) PLE_FWD_P1(4)
+        PLE_FWD_P1(5) PLE_FWD_P1(6) PLE_FWD_P1(7) PLE_FWD_P1(8)
+#undef PLE_FWD_P1
+        default: break;
       }
       __syncthreads();
       // ---- phase 2: output chunks of this thread's column
@@ -279,14 +301,14 @@ int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cuda
   if (Fc * nc > kFwdMaxThreads) return set_error(PLE_ERR_UNSUPPORTED, "forward: d_embedding too large");
   a.lgFc = lg;
   a.n_chunks = (int)ceil_div<int64_t>(a.F, Fc);
-  int pow2 = 1;
-  while (pow2 < a.B + 1) pow2 <<= 1;
-  a.pow2 = pow2;
+  int lgk = 0;
+  while ((1 << lgk) < a.B) ++lgk;  // 2^lgk - 1 >= B - 1 interior edges
+  a.lgk = lgk;
   const int R = Fc * nc;
   const int threads = R * (kFwdMaxThreads / R);
   a.S_t = kFwdPairsPerTile / Fc;
   if (a.S_t < 1) a.S_t = 1;
-  a.ldE = pow2 + 1;  // odd row stride: the first probes of different features hit different banks
+  a.ldK = (1 << lgk) + 1;  // odd row stride: the first probes of different features hit different banks
   a.x_vec4 = (Fc >= 4) && (a.F % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
   const size_t smem = fwd_layout(a, nullptr, nullptr);
   if (smem > device_max_smem_optin())

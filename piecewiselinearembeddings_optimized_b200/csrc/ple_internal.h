@@ -35,7 +35,7 @@ struct FwdArgs {
   int F, B, D;
   int epi, relu;
   // filled by the launcher
-  int lgFc, n_chunks, S_t, pow2, ldE, x_vec4;
+  int lgFc, n_chunks, S_t, lgk, ldK, x_vec4;
 };
 
 struct BwdArgs {
@@ -62,6 +62,7 @@ struct BwdArgs {
   int epi, relu;
   // filled by the launcher (Fc = features per chunk; the sorted kernel uses 1 << lgFc)
   int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4, Fc;
+  int lgk;  // sorted kernel: 2^lgk - 1 >= B - 1 interior-edge search keys
 };
 
 struct EncArgs {

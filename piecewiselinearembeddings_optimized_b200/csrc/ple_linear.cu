@@ -12,13 +12,17 @@
 // M = 128 MMA each) by HG output columns (one column group of the H outputs).
 // The K dimension (F * D) is walked in feature groups of G features (K slice
 // KA = G * D, a multiple of 16).  Warp roles:
-//   producers (P warps)  per group: wait for the group's tables; phase 1, one
-//       thread per (row, feature): bin search + position -> a 16-byte record;
-//       phase 2, one thread per fixed 8-column chunk of the slice, looping over
-//       rows: two table reads, epilogue, bf16 conversion, one 16-byte store
-//       into the A slot of the stage ring (canonical K-major no-swizzle layout
-//       with a padded k-block stride, so the stores of consecutive chunks hit
-//       distinct banks); then fence.proxy.async and one arrive per warp.
+//   producers (P warps)  per group: wait for the group's tables; each thread
+//       owns a fixed 8-column chunk of the slice (inside one feature) and a
+//       fixed set of rows; per row: bin search on the feature's edges,
+//       position, two table reads, epilogue, bf16 conversion and one 16-byte
+//       store into the A slot of the stage ring (canonical K-major no-swizzle
+//       layout with a padded k-block stride, so the stores of consecutive
+//       chunks hit distinct banks); then fence.proxy.async and one arrive per
+//       warp.  The lanes of one (row, feature) repeat its bin search instead
+//       of sharing it through shared memory: no barrier ties the producer
+//       warps together, so they drift across groups and hide each other's
+//       latency; x arrives in registers one group ahead.
 //   loader (1 thread)    per group: bulk-copies the group's table image and the
 //       group's W1 slice (pre-arranged in the MMA's core-matrix layout by a
 //       pre-pass) into the table ring and the stage ring.
@@ -33,9 +37,13 @@
 //
 // Table image of a feature group (built per call from W by a pre-pass, the
 // same prefix / slope tables as the fused forward):
-//   n[G] i32 | edges[G][pow2 + 1] f32 (+inf padded) | inv_w[G][B] f32 |
+//   n[G] i32 | keys[G][2^L] f32 | left[G][B] {e_k, r_k} f32x2 |
 //   epi[2][KA] f32 (bias, or w0 and b0) | T[B][ldT] f32 | S[B][ldS] ST
-// with T[k][f*D + d] = sum_{j<k} q(W[f, j, d]) and S[k][..] = q(W[f, phys k, d]);
+// with keys = the interior edges e_1 .. e_{n-1} then +inf (2^L - 1 used, 2^L >= B),
+// T[k][f*D + d] = sum_{j<k} q(W[f, j, d]) and S[k][..] = q(W[f, phys k, d]).
+// The count of keys <= x, capped at n - 1, is the clamped right-sided bin
+// (x below e_0 counts no key, x at or above e_n counts n - 1, NaN counts every
+// key): an L-probe search instead of L + 2 over all B + 1 edges.
 // the T and S rows are padded to a multiple of 128 bytes so that the reads of
 // lanes on different bins fall on the same bank pattern.
 #include <stdio.h>
@@ -56,18 +64,18 @@ __device__ int g_lin_dev_err = 0;
 
 constexpr int kLinLBO = 144;             // A slot: byte step between k-blocks (128-byte core matrix + 16)
 constexpr int kLinWaitLimit = 1 << 22;   // polls per wait
-constexpr int kLinMaxIP = 4;             // phase-1 items per producer thread
-constexpr int kLinMaxThreads = 448;      // 12 producer warps + loader + MMA
+constexpr int kLinMaxRows = 8;           // rows per producer thread and group
+constexpr int kLinMaxThreads = 576;      // up to 16 producer warps + loader + MMA
 // Planning budget: the sm_100 opt-in maximum of dynamic shared memory per CTA (a
 // constant, so that workspace sizes do not depend on which device is queried).
 constexpr size_t kLinSmemBudget = 227 * 1024;
 
 struct LinGeom {
-  int G, lgG, KA, R, P, RS, rows, HG, n_hg, Nm, n_nm, SA, ST, IP;
-  int n_groups, pow2, ldE, ldT, ldS;  // ldT floats, ldS elements of the slope type
+  int G, KA, R, P, RS, rows, HG, n_hg, Nm, n_nm, SA, ST, NR;
+  int n_groups, lgk, ldK, ldT, ldS;   // keys per feature 2^lgk; ldT floats, ldS elements of the slope type
   int TB, WB, AB, SBO_A;              // bytes
-  int oN, oE, oR, oEp, oT, oS;        // byte offsets inside a table slot
-  int oTab, oStage, oRec, oBar, smem; // byte offsets in dynamic shared memory
+  int oN, oK, oL, oEp, oT, oS;        // byte offsets inside a table slot
+  int oTab, oStage, oBar, smem;       // byte offsets in dynamic shared memory
   int tmem_cols;
 };
 
@@ -99,8 +107,8 @@ __global__ void ple_lin_tables_kernel(const float* __restrict__ edges, const flo
   const int f0 = gi * G;
   unsigned char* base = img + (int64_t)gi * g.TB;
   int* sN = reinterpret_cast<int*>(base + g.oN);
-  float* sE = reinterpret_cast<float*>(base + g.oE);
-  float* sR = reinterpret_cast<float*>(base + g.oR);
+  float* sK = reinterpret_cast<float*>(base + g.oK);
+  float2* sL = reinterpret_cast<float2*>(base + g.oL);
   float* sEp = reinterpret_cast<float*>(base + g.oEp);
   float* sT = reinterpret_cast<float*>(base + g.oT);
   ST* sS = reinterpret_cast<ST*>(base + g.oS);
@@ -109,21 +117,20 @@ __global__ void ple_lin_tables_kernel(const float* __restrict__ edges, const flo
     const int n = n_bins[f];
     return n < 1 ? 1 : (n > B ? B : n);
   };
-  for (int i = threadIdx.x; i < (g.oE - g.oN) / 4; i += blockDim.x) sN[i] = i < G ? nb(f0 + i) : 0;
-  // padding features (f >= F): edges {0, +inf, ...} and zero widths, so x = 0 gives k = 0 and t = 0
-  for (int idx = threadIdx.x; idx < G * g.ldE; idx += blockDim.x) {
-    const int i = idx / g.ldE, j = idx - i * g.ldE, f = f0 + i;
+  for (int i = threadIdx.x; i < (g.oK - g.oN) / 4; i += blockDim.x) sN[i] = i < G ? nb(f0 + i) : 0;
+  // keys: interior edges e_1 .. e_{n-1}, +inf after (padding features: no keys)
+  for (int idx = threadIdx.x; idx < G * g.ldK; idx += blockDim.x) {
+    const int i = idx / g.ldK, j = idx - i * g.ldK, f = f0 + i;
     float e = __int_as_float(0x7f800000);
-    if (f < F) {
-      if (j <= nb(f)) e = edges[(int64_t)f * (B + 1) + j];
-    } else if (j == 0) {
-      e = 0.0f;
-    }
-    sE[idx] = e;
+    if (f < F && j + 1 < nb(f)) e = edges[(int64_t)f * (B + 1) + j + 1];
+    sK[idx] = e;
   }
+  // {e_k, r_k} of each real bin; padding features and bins {0, 0}, so x = 0 gives t = 0 there
   for (int idx = threadIdx.x; idx < G * B; idx += blockDim.x) {
     const int i = idx / B, j = idx - i * B, f = f0 + i;
-    sR[idx] = (f < F && j < nb(f)) ? inv_w[(int64_t)f * B + j] : 0.0f;
+    float2 v = make_float2(0.0f, 0.0f);
+    if (f < F && j < nb(f)) v = make_float2(edges[(int64_t)f * (B + 1) + j], inv_w[(int64_t)f * B + j]);
+    sL[idx] = v;
   }
   for (int c = threadIdx.x; c < KA; c += blockDim.x) {
     const int i = c / D, d = c - i * D, f = f0 + i;
@@ -208,21 +215,6 @@ __device__ __forceinline__ bool lin_wait(uint64_t* bar, uint32_t parity, volatil
   return false;
 }
 
-__device__ __forceinline__ void lin_named_sync(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
-// Named barrier 1 over the producer threads; returns the OR of every participant's flag.
-__device__ __forceinline__ bool lin_named_sync_or(int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(n)
-      : "memory");
-  return r != 0;
-}
-
 template <typename ZT>
 __device__ __forceinline__ void store_z8(ZT* p, int64_t h, int64_t H, const float (&v)[8]) {
   if (h + 8 <= H && (H & 7) == 0) {
@@ -236,6 +228,40 @@ __device__ __forceinline__ void store_z8(ZT* p, int64_t h, int64_t H, const floa
   } else {
     for (int e = 0; e < 8; ++e)
       if (h + e < H) p[e] = Dt<ZT>::from_f(v[e]);
+  }
+}
+
+// One producer thread's rows of one feature group: bin search over the
+// feature's interior edges, prefix / slope table reads, epilogue, bf16
+// conversion and the 16-byte store into the A slot (row i at aS + i * a_step).
+template <int LG, typename QT, typename OTe, int EPI, bool RELU, typename ST>
+__device__ __forceinline__ void lin_rows(const float (&xc)[kLinMaxRows], int nr, int n_f, const float* keys,
+                                         const float2* left, const float* sT, const ST* sS, int ldT, int ldS,
+                                         const FV<8>& ep0, const FV<8>& ep1, unsigned char* aS, int a_step) {
+#pragma unroll
+  for (int i = 0; i < kLinMaxRows; ++i) {
+    if (i < nr) {
+      const float xv = xc[i];
+      const int c = key_count<LG>(xv, keys);
+      const int k = c < n_f - 1 ? c : n_f - 1;
+      const float2 er = left[k];
+      const float tq = quantize<QT>((xv - er.x) * er.y);
+      const FV<8> tv = lds<8>(sT + k * ldT);
+      FV<8> sv;
+      if constexpr (std::is_same<ST, float>::value) {
+        sv = lds<8>(sS + k * ldS);
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(sS + k * ldS);
+        widen_pack<__nv_bfloat16>(u.x, sv.v[0], sv.v[1]);
+        widen_pack<__nv_bfloat16>(u.y, sv.v[2], sv.v[3]);
+        widen_pack<__nv_bfloat16>(u.z, sv.v[4], sv.v[5]);
+        widen_pack<__nv_bfloat16>(u.w, sv.v[6], sv.v[7]);
+      }
+      const FV<8> y = fwd_chunk<QT, OTe, 8, EPI, RELU>(tq, tv, sv, xv, ep0, ep1);
+      const uint4 pk = make_uint4(cvt_pack<__nv_bfloat16>(y.v[0], y.v[1]), cvt_pack<__nv_bfloat16>(y.v[2], y.v[3]),
+                                  cvt_pack<__nv_bfloat16>(y.v[4], y.v[5]), cvt_pack<__nv_bfloat16>(y.v[6], y.v[7]));
+      *reinterpret_cast<uint4*>(aS + i * a_step) = pk;
+    }
   }
 }
 
@@ -280,66 +306,47 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
 
   if (warp < P) {
     // ------------------------------------------------------------ producers
-    const int rows = g.rows, G = g.G, lgG = g.lgG, KA = g.KA, B = a.B, F = a.F, D = a.D;
-    const int pow2 = g.pow2, ldE = g.ldE, ldT = g.ldT, ldS = g.ldS, IP = g.IP;
-    const int npairs = rows << lgG;
+    const int rows = g.rows, G = g.G, KA = g.KA, B = a.B, F = a.F, D = a.D, lgk = g.lgk;
+    const int ldK = g.ldK, ldT = g.ldT, ldS = g.ldS, TB = g.TB, stage_bytes = g.AB + g.WB;
     const int64_t N = a.N;
-    // phase-1 items: p = tid + i * nprod -> (row p >> lgG, feature p & (G - 1)); x kept two groups ahead
-    float xa[kLinMaxIP], xb[kLinMaxIP];
-    auto load_x = [&](int gi, float (&dst)[kLinMaxIP]) {
-#pragma unroll
-      for (int i = 0; i < kLinMaxIP; ++i) {
-        dst[i] = 0.0f;
-        const int p = tid + i * nprod;
-        if (i < IP && p < npairs && gi < n_groups) {
-          const int fg = gi * G + (p & (G - 1));
-          int64_t row = row0 + (p >> lgG);
-          row = row < N ? row : N - 1;
-          if (fg < F) dst[i] = __ldg(a.x + row * F + fg);
-        }
-      }
-    };
-    load_x(0, xa);
-    load_x(1, xb);
-    // phase-2 column: 8 consecutive K columns of the slice (inside one feature, D % 8 == 0)
+    // this thread's fixed chunk: 8 consecutive K columns of the slice (inside feature cf of the group,
+    // D % 8 == 0), for rows rstart + i * rstep (rstep is a multiple of 8)
     const int R = g.R;
     const int col = tid % R, rstart = tid / R, rstep = nprod / R;
     const int cf = (col * 8) / D;
-    const int SBO_A = g.SBO_A;
+    const int nr = (rows - rstart + rstep - 1) / rstep;                 // rows of this thread
+    const int64_t nv64 = (N - row0 - rstart + rstep - 1) / rstep;        // of them inside the batch
+    const int nvalid = nv64 < nr ? (int)nv64 : nr;
+    const int a_step = (rstep >> 3) * g.SBO_A;
+    const int a_off = col * kLinLBO + (rstart >> 3) * g.SBO_A + (rstart & 7) * 16;
+    const int64_t x_step = (int64_t)rstep * F;
+    const float* xp = a.x + (row0 + rstart) * F + cf;  // advanced by G per group
+    // x of this thread's rows at feature gi * G + cf, one group ahead
+    float xc[kLinMaxRows], xn[kLinMaxRows];
+    auto load_x = [&](int gi, float (&dst)[kLinMaxRows]) {
+      const bool live = gi < n_groups && gi * G + cf < F;
+      const float* q = xp + (int64_t)gi * G;
+#pragma unroll
+      for (int i = 0; i < kLinMaxRows; ++i) dst[i] = (live && i < nvalid) ? __ldg(q + i * x_step) : 0.0f;
+    };
+    load_x(0, xc);
+    load_x(1, xn);
     bool fail = false;
-    bool stop = false;
+    int s = 0, s_round = 0, t = 0;
+    uint32_t t_par = 0;
     for (int gi = 0; gi < n_groups; ++gi) {
-      const int t = gi % STn, s = gi % SA, buf = gi & 1;
-      const unsigned char* tb = smem + g.oTab + t * g.TB;
-      float4* rec = reinterpret_cast<float4*>(smem + g.oRec) + buf * npairs;
-      if (!fail) fail = !lin_wait(&tfull[t], (gi / STn) & 1, sAbort);
-      if (!fail) {
-        const int* sN = reinterpret_cast<const int*>(tb + g.oN);
-        const float* sE = reinterpret_cast<const float*>(tb + g.oE);
-        const float* sR = reinterpret_cast<const float*>(tb + g.oR);
-#pragma unroll
-        for (int i = 0; i < kLinMaxIP; ++i) {
-          const int p = tid + i * nprod;
-          if (i < IP && p < npairs) {
-            const int f = p & (G - 1);
-            const float xv = xa[i];
-            const float* erow = sE + f * ldE;
-            const int k = logical_bin(edge_count_row(xv, erow, pow2), sN[f]);
-            const float tt = (xv - erow[k]) * sR[f * B + k];
-            rec[p] = make_float4(__int_as_float(k), quantize<QT>(tt), xv, 0.0f);
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kLinMaxIP; ++i) xa[i] = xb[i];
-      load_x(gi + 2, xb);
-      // records of this group visible; a failure anywhere stops every producer here
-      if (lin_named_sync_or(nprod, fail)) {
-        stop = true;
+      const unsigned char* tb = smem + g.oTab + t * TB;
+      bool ok = lin_wait(&tfull[t], t_par, sAbort);
+      if (ok && s_round > 0) ok = lin_wait(&empty[s], (s_round - 1) & 1, sAbort);
+      if (__any_sync(0xffffffffu, !ok)) {  // warp-uniform exit
+        fail = true;
         break;
       }
-      if (gi >= SA) fail = !lin_wait(&empty[s], ((gi / SA) - 1) & 1, sAbort);
-      if (!fail) {
+      {
+        // each lane finds the bin of its own (row, feature): no records, no barrier between the warps
+        const int n_f = reinterpret_cast<const int*>(tb + g.oN)[cf];
+        const float* keys = reinterpret_cast<const float*>(tb + g.oK) + cf * ldK;
+        const float2* left = reinterpret_cast<const float2*>(tb + g.oL) + cf * B;
         const float* sT = reinterpret_cast<const float*>(tb + g.oT) + col * 8;
         const ST* sS = reinterpret_cast<const ST*>(tb + g.oS) + col * 8;
         const float* sEp = reinterpret_cast<const float*>(tb + g.oEp) + col * 8;
@@ -348,40 +355,31 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
         for (int e = 0; e < 8; ++e) { ep0.v[e] = 0.0f; ep1.v[e] = 0.0f; }
         if constexpr (EPI != kEpiNone) ep0 = lds<8>(sEp);
         if constexpr (EPI == kEpiB) ep1 = lds<8>(sEp + KA);
-        unsigned char* aS = smem + g.oStage + s * (g.AB + g.WB) + col * kLinLBO;
-        const float4* rq = rec + cf;
-#pragma unroll 2
-        for (int r = rstart; r < rows; r += rstep) {
-          const float4 q = rq[r << lgG];
-          const int k = __float_as_int(q.x);
-          const FV<8> tv = lds<8>(sT + k * ldT);
-          FV<8> sv;
-          if constexpr (std::is_same<ST, float>::value) {
-            sv = lds<8>(sS + k * ldS);
-          } else {
-            const uint4 u = *reinterpret_cast<const uint4*>(sS + k * ldS);
-            widen_pack<__nv_bfloat16>(u.x, sv.v[0], sv.v[1]);
-            widen_pack<__nv_bfloat16>(u.y, sv.v[2], sv.v[3]);
-            widen_pack<__nv_bfloat16>(u.z, sv.v[4], sv.v[5]);
-            widen_pack<__nv_bfloat16>(u.w, sv.v[6], sv.v[7]);
-          }
-          const FV<8> y = fwd_chunk<QT, OTe, 8, EPI, RELU>(q.y, tv, sv, q.z, ep0, ep1);
-          const uint4 pk = make_uint4(cvt_pack<__nv_bfloat16>(y.v[0], y.v[1]), cvt_pack<__nv_bfloat16>(y.v[2], y.v[3]),
-                                      cvt_pack<__nv_bfloat16>(y.v[4], y.v[5]), cvt_pack<__nv_bfloat16>(y.v[6], y.v[7]));
-          *reinterpret_cast<uint4*>(aS + (r >> 3) * SBO_A + (r & 7) * 16) = pk;
+        unsigned char* aS = smem + g.oStage + s * stage_bytes + a_off;
+        switch (lgk) {
+#define PLE_LIN_ROWS(L) \
+  case L: lin_rows<L, QT, OTe, EPI, RELU, ST>(xc, nr, n_f, keys, left, sT, sS, ldT, ldS, ep0, ep1, aS, a_step); break;
+          PLE_LIN_ROWS(0) PLE_LIN_ROWS(1) PLE_LIN_ROWS(2) PLE_LIN_ROWS(3) PLE_LIN_ROWS(4)
+          PLE_LIN_ROWS(5) PLE_LIN_ROWS(6) PLE_LIN_ROWS(7) PLE_LIN_ROWS(8)
+#undef PLE_LIN_ROWS
+          default: break;
         }
         tc::fence_proxy_async();
       }
+#pragma unroll
+      for (int i = 0; i < kLinMaxRows; ++i) xc[i] = xn[i];
+      load_x(gi + 2, xn);
       __syncwarp();
       if (lane == 0) {
         tc::mbar_arrive(&full[s]);
         tc::mbar_arrive(&tempty[t]);
       }
+      if (++s == SA) { s = 0; ++s_round; }
+      if (++t == STn) { t = 0; t_par ^= 1u; }
     }
-    if (!stop) stop = lin_named_sync_or(nprod, fail);
     // ------------------------------------------------------------ epilogue: TMEM -> z
-    if (!stop) {
-      const bool ok = __all_sync(0xffffffffu, lin_wait(accb, 0, sAbort));
+    if (!fail) {
+      const bool ok = __all_sync(0xffffffffu, lin_wait(accb, 0, sAbort)) && *sAbort == 0;
       if (ok) {
         tc::fence_after_sync();
         const int q = warp & 3;
@@ -411,8 +409,8 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
         }
       }
     }
-    if (fail || stop) {
-      if (tid == 0) atomicExch(a.dev_err, 1);
+    if (fail || *sAbort) {
+      if (lane == 0) atomicExch(a.dev_err, 1);
     }
   } else if (warp == P) {
     // ------------------------------------------------------------ loader
@@ -483,11 +481,6 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
 }
 
 // ------------------------------------------------------------------ host
-static int pow2_ceil(int v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 // Geometry for (F, B, D, H) and the slope element size; false when no
@@ -495,8 +488,10 @@ static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 static bool lin_plan(int F, int B, int D, int64_t H, int s_bytes, size_t smem_max, LinGeom* out) {
   if (D % 8 != 0 || H <= 0 || H > (1 << 20)) return false;
   LinGeom g{};
-  g.pow2 = pow2_ceil(B + 1);
-  g.ldE = g.pow2 + 1;
+  g.lgk = 0;
+  while ((1 << g.lgk) < B) ++g.lgk;  // 2^lgk - 1 >= B - 1 interior edges
+  if (g.lgk > 8) return false;
+  g.ldK = 1 << g.lgk;
   const int Hp = round_up((int)H, 16);
   struct Cn { int RS, HG, n_hg, n_nm; };
   Cn cands[2];
@@ -515,23 +510,24 @@ static bool lin_plan(int F, int B, int D, int64_t H, int s_bytes, size_t smem_ma
       if (KA % 16 != 0 || KA > 128) continue;
       const int R = KA / 8;
       int P = 0;
-      for (int p = 12; p >= 4; --p)
-        if ((32 * p) % R == 0) { P = p; break; }
+      for (int p = 16; p >= 4; --p)
+        if ((32 * p) % R == 0 && ((32 * p) / R) % 8 == 0) { P = p; break; }
       if (P == 0) continue;
       const int rows = 128 * cands[ci].RS;
-      const int IP = (rows * G + 32 * P - 1) / (32 * P);
-      if (IP > kLinMaxIP) continue;
+      const int rstep = 32 * P / R;
+      const int NR = (rows + rstep - 1) / rstep;
+      if (NR > kLinMaxRows || rstep % 8 != 0) continue;
       LinGeom c = g;
-      c.G = G; c.lgG = G == 8 ? 3 : G == 4 ? 2 : G == 2 ? 1 : 0;
-      c.KA = KA; c.R = R; c.P = P; c.RS = cands[ci].RS; c.rows = rows; c.IP = IP;
+      c.G = G;
+      c.KA = KA; c.R = R; c.P = P; c.RS = cands[ci].RS; c.rows = rows; c.NR = NR;
       c.HG = cands[ci].HG; c.n_hg = cands[ci].n_hg; c.n_nm = cands[ci].n_nm; c.Nm = c.HG / c.n_nm;
       c.n_groups = (F + G - 1) / G;
       c.ldT = round_up(KA, 32);
       c.ldS = round_up(KA * s_bytes, 128) / s_bytes;
       int off = 0;
       c.oN = off; off += round_up(G * 4, 16);
-      c.oE = off; off += round_up(G * c.ldE * 4, 16);
-      c.oR = off; off += round_up(G * B * 4, 16);
+      c.oK = off; off += round_up(G * c.ldK * 4, 16);
+      c.oL = off; off += round_up(G * B * 8, 16);
       c.oEp = off; off += round_up(2 * KA * 4, 16);
       c.oT = off; off += B * c.ldT * 4;
       c.oS = off; off += B * c.ldS * s_bytes;
@@ -543,19 +539,20 @@ static bool lin_plan(int F, int B, int D, int64_t H, int s_bytes, size_t smem_ma
       while (c.tmem_cols < c.RS * c.HG) c.tmem_cols <<= 1;
       if (c.tmem_cols > 512) continue;
       for (int SA = 3; SA >= 2; --SA) {
-        c.SA = SA;
-        c.ST = 2;
-        int o = 0;
-        c.oStage = o; o += SA * (c.AB + c.WB);
-        c.oTab = o; o += c.ST * c.TB;
-        c.oRec = o; o += 2 * rows * G * 16;
-        c.oBar = o; o += (3 * SA + 2 * c.ST + 1) * 8 + 16;
-        c.smem = round_up(o, 128);
-        // at least 116 KB keeps one CTA per SM (the whole tensor memory is available to it)
-        if (c.smem < 116 * 1024) c.smem = 116 * 1024;
-        if ((size_t)c.smem <= smem_max) {
-          *out = c;
-          return true;
+        for (int STn = 4; STn >= 2; --STn) {
+          c.SA = SA;
+          c.ST = STn;
+          int o = 0;
+          c.oStage = o; o += SA * (c.AB + c.WB);
+          c.oTab = o; o += c.ST * c.TB;
+          c.oBar = o; o += (3 * SA + 2 * c.ST + 1) * 8 + 16;
+          c.smem = round_up(o, 128);
+          // at least 116 KB keeps one CTA per SM (the whole tensor memory is available to it)
+          if (c.smem < 116 * 1024) c.smem = 116 * 1024;
+          if ((size_t)c.smem <= smem_max) {
+            *out = c;
+            return true;
+          }
         }
       }
     }
