@@ -12,17 +12,17 @@
 // M = 128 MMA each) by HG output columns (one column group of the H outputs).
 // The K dimension (F * D) is walked in feature groups of G features (K slice
 // KA = G * D, a multiple of 16).  Warp roles:
-//   producers (P warps)  per group: wait for the group's tables; each thread
-//       owns a fixed 8-column chunk of the slice (inside one feature) and a
-//       fixed set of rows; per row: bin search on the feature's edges,
-//       position, two table reads, epilogue, bf16 conversion and one 16-byte
-//       store into the A slot of the stage ring (canonical K-major no-swizzle
-//       layout with a padded k-block stride, so the stores of consecutive
-//       chunks hit distinct banks); then fence.proxy.async and one arrive per
-//       warp.  The lanes of one (row, feature) repeat its bin search instead
-//       of sharing it through shared memory: no barrier ties the producer
-//       warps together, so they drift across groups and hide each other's
-//       latency; x arrives in registers one group ahead.
+//   producers (P warps)  per group: wait for the group's tables; the work is
+//       cut into items of 32 consecutive rows (one per lane) of one feature;
+//       per item each lane runs one L-probe bin search over the feature's
+//       interior edges, reads {e_k, r_k}, then for each 8-column chunk of the
+//       feature two table rows, applies the epilogue, converts to bf16 and
+//       stores 16 bytes into the A slot of the stage ring (canonical K-major
+//       no-swizzle layout: the 32 lanes' stores of one chunk fill four whole
+//       128-byte core-matrix rows); then fence.proxy.async and one arrive per
+//       warp.  No barrier ties the producer warps together; the table rows
+//       are skewed by 16 bytes per bin so that lanes on different bins
+//       spread over the banks; x arrives in registers one group ahead.
 //   loader (1 thread)    per group: bulk-copies the group's table image and the
 //       group's W1 slice (pre-arranged in the MMA's core-matrix layout by a
 //       pre-pass) into the table ring and the stage ring.
@@ -39,13 +39,14 @@
 // same prefix / slope tables as the fused forward):
 //   n[G] i32 | keys[G][2^L] f32 | left[G][B] {e_k, r_k} f32x2 |
 //   epi[2][KA] f32 (bias, or w0 and b0) | T[B][ldT] f32 | S[B][ldS] ST
+// (T rows KA + 4 floats, S rows padded to an odd number of 16-byte units)
 // with keys = the interior edges e_1 .. e_{n-1} then +inf (2^L - 1 used, 2^L >= B),
 // T[k][f*D + d] = sum_{j<k} q(W[f, j, d]) and S[k][..] = q(W[f, phys k, d]).
 // The count of keys <= x, capped at n - 1, is the clamped right-sided bin
 // (x below e_0 counts no key, x at or above e_n counts n - 1, NaN counts every
 // key): an L-probe search instead of L + 2 over all B + 1 edges.
-// the T and S rows are padded to a multiple of 128 bytes so that the reads of
-// lanes on different bins fall on the same bank pattern.
+// the T and S row strides are an odd number of 16-byte units, so the reads of
+// lanes on different bins start in different bank groups.
 #include <stdio.h>
 #include <string.h>
 
@@ -62,16 +63,18 @@ namespace ple {
 // Set to 1 by a fused-linear launch whose wait expired (ple_linear_status reads and clears it).
 __device__ int g_lin_dev_err = 0;
 
-constexpr int kLinLBO = 144;             // A slot: byte step between k-blocks (128-byte core matrix + 16)
-constexpr int kLinWaitLimit = 1 << 22;   // polls per wait
-constexpr int kLinMaxRows = 8;           // rows per producer thread and group
+constexpr int kLinLBO = 128;             // A slot: byte step between k-blocks (canonical, packed)
+constexpr int kLinWaitLimit = 1 << 22;   // polls of the final drain waits
+constexpr uint32_t kLinSuspendNs = 2000; // suspend-time hint of one poll
+constexpr long long kLinWaitCycles = 4000000000LL;  // time bound of one wait (SM cycles)
+constexpr int kLinMaxItems = 4;          // 32-row items per producer warp and group
 constexpr int kLinMaxThreads = 576;      // up to 16 producer warps + loader + MMA
 // Planning budget: the sm_100 opt-in maximum of dynamic shared memory per CTA (a
 // constant, so that workspace sizes do not depend on which device is queried).
 constexpr size_t kLinSmemBudget = 227 * 1024;
 
 struct LinGeom {
-  int G, KA, R, P, RS, rows, HG, n_hg, Nm, n_nm, SA, ST, NR;
+  int G, KA, P, RS, rows, HG, n_hg, Nm, n_nm, SA, ST, n_items;
   int n_groups, lgk, ldK, ldT, ldS;   // keys per feature 2^lgk; ldT floats, ldS elements of the slope type
   int TB, WB, AB, SBO_A;              // bytes
   int oN, oK, oL, oEp, oT, oS;        // byte offsets inside a table slot
@@ -197,19 +200,30 @@ __global__ void ple_lin_wimg_kernel(const __nv_bfloat16* __restrict__ W1, int64_
 }
 
 // ------------------------------------------------------------------ main kernel
+// Wait for the phase of `parity` of an mbarrier.  Each poll may suspend the
+// thread in hardware for up to kLinSuspendNs (it resumes when the phase
+// completes), so waiting threads do not spin on the issue slots the producer
+// warps need.  Bounded by time: after kLinWaitCycles SM cycles (about two
+// seconds) the wait gives up and raises the CTA's abort flag; it also returns
+// early once another role has raised it.
 __device__ __forceinline__ bool lin_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t a = tc::smem_addr(bar);
-  for (int i = 0; i < kLinWaitLimit; ++i) {
+  long long t0 = 0;
+  for (int i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(kLinSuspendNs)
         : "memory");
     if (done) return true;
-    if ((i & 63) == 63 && *abort) return false;
+    if (i == 0) t0 = clock64();
+    if ((i & 7) == 7) {
+      if (*abort) return false;
+      if (clock64() - t0 > kLinWaitCycles) break;
+    }
   }
   *abort = 1;
   return false;
@@ -231,37 +245,52 @@ __device__ __forceinline__ void store_z8(ZT* p, int64_t h, int64_t H, const floa
   }
 }
 
-// One producer thread's rows of one feature group: bin search over the
-// feature's interior edges, prefix / slope table reads, epilogue, bf16
-// conversion and the 16-byte store into the A slot (row i at aS + i * a_step).
-template <int LG, typename QT, typename OTe, int EPI, bool RELU, typename ST>
-__device__ __forceinline__ void lin_rows(const float (&xc)[kLinMaxRows], int nr, int n_f, const float* keys,
-                                         const float2* left, const float* sT, const ST* sS, int ldT, int ldS,
-                                         const FV<8>& ep0, const FV<8>& ep1, unsigned char* aS, int a_step) {
+// key_count with a pointer walk: each probe is a load at an immediate offset,
+// a compare and a select.
+template <int L>
+__device__ __forceinline__ int key_count_ptr(float x, const float* keys) {
+  const float* p = keys;
 #pragma unroll
-  for (int i = 0; i < kLinMaxRows; ++i) {
-    if (i < nr) {
-      const float xv = xc[i];
-      const int c = key_count<LG>(xv, keys);
-      const int k = c < n_f - 1 ? c : n_f - 1;
-      const float2 er = left[k];
-      const float tq = quantize<QT>((xv - er.x) * er.y);
-      const FV<8> tv = lds<8>(sT + k * ldT);
-      FV<8> sv;
-      if constexpr (std::is_same<ST, float>::value) {
-        sv = lds<8>(sS + k * ldS);
-      } else {
-        const uint4 u = *reinterpret_cast<const uint4*>(sS + k * ldS);
-        widen_pack<__nv_bfloat16>(u.x, sv.v[0], sv.v[1]);
-        widen_pack<__nv_bfloat16>(u.y, sv.v[2], sv.v[3]);
-        widen_pack<__nv_bfloat16>(u.z, sv.v[4], sv.v[5]);
-        widen_pack<__nv_bfloat16>(u.w, sv.v[6], sv.v[7]);
-      }
-      const FV<8> y = fwd_chunk<QT, OTe, 8, EPI, RELU>(tq, tv, sv, xv, ep0, ep1);
-      const uint4 pk = make_uint4(cvt_pack<__nv_bfloat16>(y.v[0], y.v[1]), cvt_pack<__nv_bfloat16>(y.v[2], y.v[3]),
-                                  cvt_pack<__nv_bfloat16>(y.v[4], y.v[5]), cvt_pack<__nv_bfloat16>(y.v[6], y.v[7]));
-      *reinterpret_cast<uint4*>(aS + i * a_step) = pk;
+  for (int h = (1 << L) >> 1; h > 0; h >>= 1) p = !(x < p[h - 1]) ? p + h : p;
+  return (int)(p - keys);
+}
+
+// One item of a producer warp: this lane's row of one feature of the group.
+// Bin search over the feature's interior edges, position, then per 8-column
+// chunk the prefix / slope rows, the epilogue, bf16 conversion and a 16-byte
+// store into the A slot (chunk cc at aS + cc * 128).  sT, sS, sEp point at the
+// feature's first column.
+template <int L, typename QT, typename OTe, int EPI, bool RELU, typename ST>
+__device__ __forceinline__ void lin_item(float xv, int n_f, const float* keys, const float2* left, const float* sT,
+                                         const ST* sS, const float* sEp, int ldT, int ldS, int KA, int nd,
+                                         unsigned char* aS) {
+  const int c = key_count_ptr<L>(xv, keys);
+  const int k = c < n_f - 1 ? c : n_f - 1;
+  const float2 er = left[k];
+  const float tq = quantize<QT>((xv - er.x) * er.y);
+  const float* tr = sT + k * ldT;
+  const ST* sr = sS + k * ldS;
+  for (int cc = 0; cc < nd; ++cc) {
+    FV<8> ep0, ep1;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { ep0.v[e] = 0.0f; ep1.v[e] = 0.0f; }
+    if constexpr (EPI != kEpiNone) ep0 = lds<8>(sEp + cc * 8);
+    if constexpr (EPI == kEpiB) ep1 = lds<8>(sEp + KA + cc * 8);
+    const FV<8> tv = lds<8>(tr + cc * 8);
+    FV<8> sv;
+    if constexpr (std::is_same<ST, float>::value) {
+      sv = lds<8>(sr + cc * 8);
+    } else {
+      const uint4 u = *reinterpret_cast<const uint4*>(sr + cc * 8);
+      widen_pack<__nv_bfloat16>(u.x, sv.v[0], sv.v[1]);
+      widen_pack<__nv_bfloat16>(u.y, sv.v[2], sv.v[3]);
+      widen_pack<__nv_bfloat16>(u.z, sv.v[4], sv.v[5]);
+      widen_pack<__nv_bfloat16>(u.w, sv.v[6], sv.v[7]);
     }
+    const FV<8> y = fwd_chunk<QT, OTe, 8, EPI, RELU>(tq, tv, sv, xv, ep0, ep1);
+    const uint4 pk = make_uint4(cvt_pack<__nv_bfloat16>(y.v[0], y.v[1]), cvt_pack<__nv_bfloat16>(y.v[2], y.v[3]),
+                                cvt_pack<__nv_bfloat16>(y.v[4], y.v[5]), cvt_pack<__nv_bfloat16>(y.v[6], y.v[7]));
+    *reinterpret_cast<uint4*>(aS + cc * kLinLBO) = pk;
   }
 }
 
@@ -272,7 +301,7 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
   extern __shared__ __align__(1024) unsigned char smem[];
   const LinGeom& g = a.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int P = g.P, nprod = 32 * P, SA = g.SA, STn = g.ST, n_groups = g.n_groups;
+  const int P = g.P, SA = g.SA, STn = g.ST, n_groups = g.n_groups;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + g.oBar);
   uint64_t* full = bars;              // [SA] producer warps wrote the A slot
   uint64_t* wfull = bars + SA;        // [SA] W1 slice landed
@@ -306,28 +335,27 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
 
   if (warp < P) {
     // ------------------------------------------------------------ producers
-    const int rows = g.rows, G = g.G, KA = g.KA, B = a.B, F = a.F, D = a.D, lgk = g.lgk;
+    const int G = g.G, KA = g.KA, B = a.B, F = a.F, D = a.D, lgk = g.lgk;
     const int ldK = g.ldK, ldT = g.ldT, ldS = g.ldS, TB = g.TB, stage_bytes = g.AB + g.WB;
     const int64_t N = a.N;
-    // this thread's fixed chunk: 8 consecutive K columns of the slice (inside feature cf of the group,
-    // D % 8 == 0), for rows rstart + i * rstep (rstep is a multiple of 8)
-    const int R = g.R;
-    const int col = tid % R, rstart = tid / R, rstep = nprod / R;
-    const int cf = (col * 8) / D;
-    const int nr = (rows - rstart + rstep - 1) / rstep;                 // rows of this thread
-    const int64_t nv64 = (N - row0 - rstart + rstep - 1) / rstep;        // of them inside the batch
-    const int nvalid = nv64 < nr ? (int)nv64 : nr;
-    const int a_step = (rstep >> 3) * g.SBO_A;
-    const int a_off = col * kLinLBO + (rstart >> 3) * g.SBO_A + (rstart & 7) * 16;
-    const int64_t x_step = (int64_t)rstep * F;
-    const float* xp = a.x + (row0 + rstart) * F + cf;  // advanced by G per group
-    // x of this thread's rows at feature gi * G + cf, one group ahead
-    float xc[kLinMaxRows], xn[kLinMaxRows];
-    auto load_x = [&](int gi, float (&dst)[kLinMaxRows]) {
-      const bool live = gi < n_groups && gi * G + cf < F;
-      const float* q = xp + (int64_t)gi * G;
+    // items of this warp: it = warp + j * P -> rows rb * 32 + lane of feature f = it % G of the group
+    const int nd = D / 8, n_items = g.n_items, SBO_A = g.SBO_A;
+    const int my_items = warp < n_items ? (n_items - warp + P - 1) / P : 0;
+    const unsigned char* tab0 = smem + g.oTab;
+    unsigned char* stage0 = smem + g.oStage;
+    // x of this lane's rows, one group ahead
+    float xc[kLinMaxItems], xn[kLinMaxItems];
+    auto load_x = [&](int gi, float (&dst)[kLinMaxItems]) {
 #pragma unroll
-      for (int i = 0; i < kLinMaxRows; ++i) dst[i] = (live && i < nvalid) ? __ldg(q + i * x_step) : 0.0f;
+      for (int j = 0; j < kLinMaxItems; ++j) {
+        dst[j] = 0.0f;
+        if (j < my_items && gi < n_groups) {
+          const int it = warp + j * P, rb = it / G, f = it - rb * G;
+          const int64_t row = row0 + rb * 32 + lane;
+          const int fg = gi * G + f;
+          if (row < N && fg < F) dst[j] = __ldg(a.x + row * F + fg);
+        }
+      }
     };
     load_x(0, xc);
     load_x(1, xn);
@@ -335,39 +363,39 @@ __global__ void __launch_bounds__(kLinMaxThreads, 1) ple_linear_kernel(const __g
     int s = 0, s_round = 0, t = 0;
     uint32_t t_par = 0;
     for (int gi = 0; gi < n_groups; ++gi) {
-      const unsigned char* tb = smem + g.oTab + t * TB;
+      const unsigned char* tb = tab0 + t * TB;
       bool ok = lin_wait(&tfull[t], t_par, sAbort);
       if (ok && s_round > 0) ok = lin_wait(&empty[s], (s_round - 1) & 1, sAbort);
       if (__any_sync(0xffffffffu, !ok)) {  // warp-uniform exit
         fail = true;
         break;
       }
-      {
-        // each lane finds the bin of its own (row, feature): no records, no barrier between the warps
-        const int n_f = reinterpret_cast<const int*>(tb + g.oN)[cf];
-        const float* keys = reinterpret_cast<const float*>(tb + g.oK) + cf * ldK;
-        const float2* left = reinterpret_cast<const float2*>(tb + g.oL) + cf * B;
-        const float* sT = reinterpret_cast<const float*>(tb + g.oT) + col * 8;
-        const ST* sS = reinterpret_cast<const ST*>(tb + g.oS) + col * 8;
-        const float* sEp = reinterpret_cast<const float*>(tb + g.oEp) + col * 8;
-        FV<8> ep0, ep1;
+      unsigned char* slot = stage0 + s * stage_bytes;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { ep0.v[e] = 0.0f; ep1.v[e] = 0.0f; }
-        if constexpr (EPI != kEpiNone) ep0 = lds<8>(sEp);
-        if constexpr (EPI == kEpiB) ep1 = lds<8>(sEp + KA);
-        unsigned char* aS = smem + g.oStage + s * stage_bytes + a_off;
-        switch (lgk) {
-#define PLE_LIN_ROWS(L) \
-  case L: lin_rows<L, QT, OTe, EPI, RELU, ST>(xc, nr, n_f, keys, left, sT, sS, ldT, ldS, ep0, ep1, aS, a_step); break;
-          PLE_LIN_ROWS(0) PLE_LIN_ROWS(1) PLE_LIN_ROWS(2) PLE_LIN_ROWS(3) PLE_LIN_ROWS(4)
-          PLE_LIN_ROWS(5) PLE_LIN_ROWS(6) PLE_LIN_ROWS(7) PLE_LIN_ROWS(8)
-#undef PLE_LIN_ROWS
-          default: break;
+      for (int j = 0; j < kLinMaxItems; ++j) {
+        if (j < my_items) {
+          const int it = warp + j * P, rb = it / G, f = it - rb * G;
+          const int r = rb * 32 + lane;
+          const int n_f = reinterpret_cast<const int*>(tb + g.oN)[f];
+          const float* keys = reinterpret_cast<const float*>(tb + g.oK) + f * ldK;
+          const float2* left = reinterpret_cast<const float2*>(tb + g.oL) + f * B;
+          const float* sT = reinterpret_cast<const float*>(tb + g.oT) + f * D;
+          const ST* sS = reinterpret_cast<const ST*>(tb + g.oS) + f * D;
+          const float* sEp = reinterpret_cast<const float*>(tb + g.oEp) + f * D;
+          unsigned char* aS = slot + (r >> 3) * SBO_A + (r & 7) * 16 + f * nd * kLinLBO;
+          switch (lgk) {
+#define PLE_LIN_ITEM(L) \
+  case L: lin_item<L, QT, OTe, EPI, RELU, ST>(xc[j], n_f, keys, left, sT, sS, sEp, ldT, ldS, KA, nd, aS); break;
+            PLE_LIN_ITEM(0) PLE_LIN_ITEM(1) PLE_LIN_ITEM(2) PLE_LIN_ITEM(3) PLE_LIN_ITEM(4)
+            PLE_LIN_ITEM(5) PLE_LIN_ITEM(6) PLE_LIN_ITEM(7) PLE_LIN_ITEM(8)
+#undef PLE_LIN_ITEM
+            default: break;
+          }
         }
-        tc::fence_proxy_async();
       }
+      tc::fence_proxy_async();
 #pragma unroll
-      for (int i = 0; i < kLinMaxRows; ++i) xc[i] = xn[i];
+      for (int j = 0; j < kLinMaxItems; ++j) xc[j] = xn[j];
       load_x(gi + 2, xn);
       __syncwarp();
       if (lane == 0) {
@@ -508,22 +536,17 @@ static bool lin_plan(int F, int B, int D, int64_t H, int s_bytes, size_t smem_ma
     for (int G = 8; G >= 1; G >>= 1) {
       const int KA = G * D;
       if (KA % 16 != 0 || KA > 128) continue;
-      const int R = KA / 8;
-      int P = 0;
-      for (int p = 16; p >= 4; --p)
-        if ((32 * p) % R == 0 && ((32 * p) / R) % 8 == 0) { P = p; break; }
-      if (P == 0) continue;
       const int rows = 128 * cands[ci].RS;
-      const int rstep = 32 * P / R;
-      const int NR = (rows + rstep - 1) / rstep;
-      if (NR > kLinMaxRows || rstep % 8 != 0) continue;
+      const int n_items = (rows / 32) * G;
+      const int P = n_items < 16 ? (n_items < 4 ? 4 : n_items) : 16;
+      if ((n_items + P - 1) / P > kLinMaxItems) continue;
       LinGeom c = g;
       c.G = G;
-      c.KA = KA; c.R = R; c.P = P; c.RS = cands[ci].RS; c.rows = rows; c.NR = NR;
+      c.KA = KA; c.P = P; c.RS = cands[ci].RS; c.rows = rows; c.n_items = n_items;
       c.HG = cands[ci].HG; c.n_hg = cands[ci].n_hg; c.n_nm = cands[ci].n_nm; c.Nm = c.HG / c.n_nm;
       c.n_groups = (F + G - 1) / G;
-      c.ldT = round_up(KA, 32);
-      c.ldS = round_up(KA * s_bytes, 128) / s_bytes;
+      c.ldT = KA + 4;                                   // KA + 4 floats: an odd number of 16-byte units
+      c.ldS = s_bytes == 2 ? KA + 8 : KA + 4;           // likewise for the slope rows
       int off = 0;
       c.oN = off; off += round_up(G * 4, 16);
       c.oK = off; off += round_up(G * c.ldK * 4, 16);
