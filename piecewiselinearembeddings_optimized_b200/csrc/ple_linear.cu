@@ -30,7 +30,7 @@
 //       KA / 16 x RS x n_nm MMAs, commits the stage back to the producers and
 //       loader; after the last group commits the accumulator barrier.
 // The producers then read the accumulators (tcgen05.ld), add b1 and store z.
-// Every wait is iteration-limited: an expired wait sets a shared abort flag
+// Every wait is bounded in time: an expired wait sets a shared abort flag
 // (the other roles stop at their next wait) and the device status word, the
 // CTA waits for its own copies and MMAs in flight, frees its tensor memory and
 // returns; ple_linear_status() reads the word.
@@ -39,14 +39,14 @@
 // same prefix / slope tables as the fused forward):
 //   n[G] i32 | keys[G][2^L] f32 | left[G][B] {e_k, r_k} f32x2 |
 //   epi[2][KA] f32 (bias, or w0 and b0) | T[B][ldT] f32 | S[B][ldS] ST
-// (T rows KA + 4 floats, S rows padded to an odd number of 16-byte units)
 // with keys = the interior edges e_1 .. e_{n-1} then +inf (2^L - 1 used, 2^L >= B),
 // T[k][f*D + d] = sum_{j<k} q(W[f, j, d]) and S[k][..] = q(W[f, phys k, d]).
 // The count of keys <= x, capped at n - 1, is the clamped right-sided bin
 // (x below e_0 counts no key, x at or above e_n counts n - 1, NaN counts every
-// key): an L-probe search instead of L + 2 over all B + 1 edges.
-// the T and S row strides are an odd number of 16-byte units, so the reads of
-// lanes on different bins start in different bank groups.
+// key): an L-probe search instead of L + 2 over all B + 1 edges.  The T and S
+// row strides (ldT = KA + 4 floats, ldS padded likewise) are an odd number of
+// 16-byte units, so the reads of lanes on different bins start in different
+// bank groups.
 #include <stdio.h>
 #include <string.h>
 
