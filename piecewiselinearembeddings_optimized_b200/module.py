@@ -160,10 +160,16 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
     bf16 for the product and the result is fp32.  Everything else (CPU inputs,
     fp16 autocast, plain fp32, d_embedding not a multiple of 8) runs the
     composition: the module's own kernel followed by ``linear``.
+
+    ``fused=False`` always runs the composition.  The trade-off: the fused
+    kernel never allocates the ``[N, F, D]`` activation (805 MB at 65,536 rows
+    × 256 features × D = 24 in bf16), but on one B200 it is currently slower
+    than the composition at the measured shapes (e.g. 0.55 ms against 0.43 ms
+    for Linear(6144, 256) over 65,536 rows); see the repository's design notes.
     """
 
     def __init__(self, embeddings: CudaPiecewiseLinearEmbeddings, linear: torch.nn.Linear, *,
-                 bf16_linear: bool = False) -> None:
+                 bf16_linear: bool = False, fused: bool = True) -> None:
         super().__init__()
         d_in = embeddings.n_features * embeddings.d_embedding
         if linear.in_features != d_in:
@@ -172,9 +178,10 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
         self.embeddings = embeddings
         self.linear = linear
         self.bf16_linear = bf16_linear
+        self.fused = fused
 
     def _fused_dtypes(self, x: Tensor):
-        if x.device.type != "cuda" or self.embeddings.d_embedding % 8 != 0:
+        if not self.fused or x.device.type != "cuda" or self.embeddings.d_embedding % 8 != 0:
             return None
         if torch.is_autocast_enabled("cuda"):
             if torch.get_autocast_dtype("cuda") != torch.bfloat16:

@@ -231,3 +231,7 @@ def test_module_bf16_linear_fp32_and_fallbacks(cuda_device):
         ref = e @ lin.weight.to(torch.bfloat16).double().t() + lin.bias.double()
         scale = e.abs() @ lin.weight.to(torch.bfloat16).double().abs().t()
         assert bool(((z.double() - ref).abs() <= 2e-3 * scale + 1e-5).all())
+        fused.fused = False  # the composition, whatever the dtypes
+        assert torch.equal(fused(x), composed)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        assert torch.equal(fused(x), lin(emb(x).flatten(1)))
