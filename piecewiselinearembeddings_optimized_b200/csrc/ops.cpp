@@ -125,6 +125,24 @@ at::Tensor workspace_for(const at::Tensor& like, int64_t N, int64_t F, int64_t B
   return at::empty({(int64_t)bytes}, like.options().dtype(at::kByte));
 }
 
+// The backward kernels hold one D row in at most one warp (D / vec <= 32 lanes with vec | D), so the
+// C ABI refuses an odd d_embedding above 32, which the reference's module accepts (D <= 64).  The
+// ops below serve those shapes by appending one zero column to grad_output, weight and the epilogue
+// parameters: with W, bias, w0, b0 and g' all zero there, the column adds exactly +0 to grad_x and
+// leaves every other column's gradients unchanged; its own gradients are dropped.
+bool backward_needs_even_d(int64_t D) { return (D & 1) != 0 && D > 32; }
+
+at::Tensor pad_d(const at::Tensor& t) { return at::constant_pad_nd(t, {0, 1}, 0).contiguous(); }
+
+std::optional<at::Tensor> pad_d(const std::optional<at::Tensor>& t) {
+  if (!t.has_value()) return t;
+  return pad_d(*t);
+}
+
+at::Tensor drop_pad_d(const at::Tensor& t, int64_t D) {
+  return t.numel() == 0 ? t : t.narrow(t.dim() - 1, 0, D).contiguous();
+}
+
 std::tuple<at::Tensor, at::Tensor> ple_backward_op(const at::Tensor& grad_output, const at::Tensor& x,
                                                    const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
                                                    const at::Tensor& n_bins, const at::Tensor& weight,
@@ -147,6 +165,11 @@ std::tuple<at::Tensor, at::Tensor> ple_backward_op(const at::Tensor& grad_output
   TORCH_CHECK(bin_indices.dim() == 2 && bin_indices.size(0) == N && bin_indices.size(1) == F,
               "bin_indices shape must be [N, F]");
   c10::cuda::CUDAGuard guard(x.device());
+  if (backward_needs_even_d(D) && N > 0 && (compute_grad_x || compute_grad_weight)) {
+    auto r = ple_backward_op(pad_d(grad_output), x, bin_edges, inv_bin_widths, n_bins, pad_d(weight), bin_indices,
+                             compute_grad_x, compute_grad_weight);
+    return {std::get<0>(r), drop_pad_d(std::get<1>(r), D)};
+  }
   at::Tensor grad_x = compute_grad_x ? at::empty_like(x) : at::empty({0}, x.options());
   at::Tensor grad_w = compute_grad_weight ? at::empty_like(weight) : at::empty({0}, weight.options());
   if (!compute_grad_x && !compute_grad_weight) return {grad_x, grad_w};
@@ -223,6 +246,14 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
   auto opt = weight.options();
   const bool want_bias = compute_grad_bias && epilogue == PLE_EPILOGUE_A;
   const bool want_l0 = compute_grad_linear0 && epilogue == PLE_EPILOGUE_B;
+  if (backward_needs_even_d(D) && N > 0 && (compute_grad_x || compute_grad_weight || want_bias || want_l0)) {
+    auto r = ple_embeddings_backward_op(pad_d(grad_output), x, bin_edges, inv_bin_widths, n_bins, pad_d(weight),
+                                        pad_d(bias), pad_d(w0), pad_d(b0), bin_indices, epilogue, activation,
+                                        compute_dtype, compute_grad_x, compute_grad_weight, compute_grad_bias,
+                                        compute_grad_linear0);
+    return {std::get<0>(r), drop_pad_d(std::get<1>(r), D), drop_pad_d(std::get<2>(r), D),
+            drop_pad_d(std::get<3>(r), D), drop_pad_d(std::get<4>(r), D)};
+  }
   at::Tensor gx = compute_grad_x ? at::empty_like(x) : at::empty({0}, x.options());
   at::Tensor gw = compute_grad_weight ? at::empty_like(weight) : at::empty({0}, opt);
   at::Tensor gb = want_bias ? at::empty({F, D}, opt) : at::empty({0}, opt);

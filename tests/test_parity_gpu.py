@@ -115,6 +115,40 @@ def test_fused_low_precision_matches_oracle(ops, cuda_device, case, version, mod
     compare_fused(res, x, edges, inv_w, nb, w, bias, w0, b0, g, version, True, mode, out_mode)
 
 
+# odd d_embedding above 32: the C ABI's backward refuses it and the torch ops pad one zero column
+@pytest.mark.parametrize("case", ["equal", "ragged", "single_bin"])
+@pytest.mark.parametrize("version", ["A", "B"])
+@pytest.mark.parametrize("d,mode,out_mode", [(33, "f32", "f32"), (63, "f32", "f32"), (45, "bf16", "bf16")])
+def test_fused_odd_wide_d_matches_oracle(ops, cuda_device, case, version, d, mode, out_mode):
+    bins = cases.make_bins(case)
+    x = cases.sample_x(bins, 96, 4000 + d)
+    edges, inv_w, nb = o.pad_bins(bins)
+    w, bias, w0, b0 = cases.init_params(len(bins), edges.shape[1] - 1, d, version, d)
+    g = o.quantize(np.random.default_rng(5000 + d).standard_normal((96, len(bins), d)).astype(np.float32), out_mode)
+    res = run_fused(ops, cuda_device, x, edges, inv_w, nb, w, bias, w0, b0, g, version, True, mode, out_mode,
+                    reuse_bins=(version == "A"))
+    assert res["grad_W"].shape == w.shape
+    compare_fused(res, x, edges, inv_w, nb, w, bias, w0, b0, g, version, True, mode, out_mode)
+
+
+@pytest.mark.parametrize("d", [33, 63])
+def test_reference_backward_odd_wide_d(ops, cuda_device, d):
+    bins = cases.make_bins("ragged")
+    x = cases.sample_x(bins, 80, 60 + d)
+    edges, inv_w, nb = o.pad_bins(bins)
+    w, *_ = cases.init_params(len(bins), edges.shape[1] - 1, d, "A", 5)
+    g = np.random.default_rng(70 + d).standard_normal((80, len(bins), d)).astype(np.float32)
+    tx, te, tr, tn, tw, tg = to_dev(cuda_device, x, edges, inv_w, nb, w, g)
+    _, idx = ops.forward(tx, te, tr, tn, tw, torch.float32)
+    gx, gw = ops.backward(tg, tx, te, tr, tn, tw, idx, True, True)
+    assert gw.shape == (len(bins), edges.shape[1] - 1, d) and gw.is_contiguous()
+    rgx, rgw, rabs = o.x_ple_backward(g, x, edges, inv_w, nb, w, "f32", with_abs=True)
+    np.testing.assert_allclose(gx.cpu().numpy(), rgx, **GRAD_TOL)
+    o.assert_reduction_close(gw.cpu().numpy(), rgw, rabs, err_msg="grad_W", **GRAD_TOL)
+    gx2, gw2 = ops.backward(tg, tx, te, tr, tn, tw, idx, False, True)
+    assert gx2.numel() == 0 and torch.equal(gw2, gw)
+
+
 # ---------------------------------------------------------------- reference-interface ops
 
 @pytest.mark.parametrize("case", cases.BIN_CASES)
