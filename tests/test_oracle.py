@@ -33,6 +33,27 @@ def test_pairwise_matches_dense(case, version, relu):
     np.testing.assert_allclose(y, yd, rtol=2e-6, atol=2e-6)
 
 
+@pytest.mark.parametrize("version", ["A", "B"])
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_zero_column_padding_leaves_gradients_unchanged(version, mode):
+    """The torch ops serve an odd d_embedding above 32 by appending one zero
+    column to g', W, bias, w0 and b0 and dropping its gradients; every other
+    gradient must come out the same."""
+    d = 33
+    x, edges, inv_w, nb, w, bias, w0, b0 = _setup("ragged", n=48, d=d, version=version, seed=11)
+    g = np.random.default_rng(12).standard_normal((48, x.shape[1], d)).astype(np.float32)
+    pad = lambda a: None if a is None else np.concatenate(  # noqa: E731
+        [a, np.zeros(a.shape[:-1] + (1,), np.float32)], axis=-1)
+    kw = dict(version=version, activation=True, mode=mode)
+    ref = o.embeddings_backward(g, x, edges, inv_w, nb, w, bias=bias, w0=w0, b0=b0, **kw)
+    got = o.embeddings_backward(pad(g), x, edges, inv_w, nb, pad(w), bias=pad(bias), w0=pad(w0), b0=pad(b0), **kw)
+    np.testing.assert_allclose(got["grad_x"], ref["grad_x"], rtol=1e-6, atol=1e-7)
+    for key in ("grad_W", "grad_bias", "grad_w0", "grad_b0"):
+        if ref.get(key) is not None:
+            assert not np.any(got[key][..., d]), key
+            np.testing.assert_array_equal(got[key][..., :d], ref[key], err_msg=key)
+
+
 def test_bin_index_rules():
     edges, inv_w, nb = o.pad_bins([np.array([0.0, 1.0, 2.0, 4.0], np.float32), np.array([-1.0, 1.0], np.float32)])
     x = np.array([[-5, -5], [0, -1], [1, 0], [1.5, 1], [2, 7], [4, np.nan], [9, np.inf],
