@@ -109,6 +109,10 @@ const char* ple_last_error_message(void);
  *   rounding through output_dtype (autocast emulation, fp32 accumulation).
  *   bin_indices[N, F] (optional, may be NULL) receives k as U8 / I16 / I32
  *   according to bin_index_dtype.
+ *   max_n_bins up to 2^20: above 256 (the reference's int16 / int32 bin-index
+ *   range) the op and ple_backward run plain global-memory kernels, correct at
+ *   any bin count but not tuned; the epilogue entry points stay at <= 256
+ *   (PLE_ERR_UNSUPPORTED above).
  */
 int ple_forward(const float* x, const float* bin_edges, const float* inv_bin_widths,
                 const int32_t* n_bins, const float* weight, int64_t batch,

@@ -130,7 +130,7 @@ at::Tensor workspace_for(const at::Tensor& like, int64_t N, int64_t F, int64_t B
 // ops below serve those shapes by appending one zero column to grad_output, weight and the epilogue
 // parameters: with W, bias, w0, b0 and g' all zero there, the column adds exactly +0 to grad_x and
 // leaves every other column's gradients unchanged; its own gradients are dropped.
-bool backward_needs_even_d(int64_t D) { return (D & 1) != 0 && D > 32; }
+bool backward_needs_even_d(int64_t B, int64_t D) { return (D & 1) != 0 && D > 32 && B <= 256; }
 
 at::Tensor pad_d(const at::Tensor& t) { return at::constant_pad_nd(t, {0, 1}, 0).contiguous(); }
 
@@ -165,7 +165,7 @@ std::tuple<at::Tensor, at::Tensor> ple_backward_op(const at::Tensor& grad_output
   TORCH_CHECK(bin_indices.dim() == 2 && bin_indices.size(0) == N && bin_indices.size(1) == F,
               "bin_indices shape must be [N, F]");
   c10::cuda::CUDAGuard guard(x.device());
-  if (backward_needs_even_d(D) && N > 0 && (compute_grad_x || compute_grad_weight)) {
+  if (backward_needs_even_d(B, D) && N > 0 && (compute_grad_x || compute_grad_weight)) {
     auto r = ple_backward_op(pad_d(grad_output), x, bin_edges, inv_bin_widths, n_bins, pad_d(weight), bin_indices,
                              compute_grad_x, compute_grad_weight);
     return {std::get<0>(r), drop_pad_d(std::get<1>(r), D)};
@@ -185,6 +185,60 @@ std::tuple<at::Tensor, at::Tensor> ple_backward_op(const at::Tensor& grad_output
   return {grad_x, grad_w};
 }
 
+// max_n_bins above 256: the C ABI serves only the bare x_ple op there (ple_wide.cu), so the module's
+// epilogue runs as ATen ops around it, in the module's order and types (module.py:230-248): x_ple in
+// the compute type, then + bias, ReLU and + linear0 in fp32; the x_ple branch of the backward gets
+// q(g' * mask) in the compute type (_autograd.py:68-80), the parameter gradients are fp32 sums.
+at::Tensor wide_pre_activation(const at::Tensor& x, const at::Tensor& bin_edges, const at::Tensor& inv_bin_widths,
+                               const at::Tensor& n_bins, const at::Tensor& weight,
+                               const std::optional<at::Tensor>& bias, int64_t epilogue,
+                               at::ScalarType compute_dtype) {
+  at::Tensor z = std::get<0>(ple_forward_op(x, bin_edges, inv_bin_widths, n_bins, weight, compute_dtype))
+                     .to(at::kFloat);
+  if (epilogue == PLE_EPILOGUE_A) {
+    TORCH_CHECK(bias.has_value(), "epilogue A needs bias");
+    z = z + *bias;
+  }
+  return z;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> wide_embeddings_backward(
+    const at::Tensor& grad_output, const at::Tensor& x, const at::Tensor& bin_edges,
+    const at::Tensor& inv_bin_widths, const at::Tensor& n_bins, const at::Tensor& weight,
+    const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& w0,
+    const std::optional<at::Tensor>& b0, int64_t epilogue, bool activation, at::ScalarType compute_dtype,
+    bool compute_grad_x, bool compute_grad_weight, bool want_bias, bool want_l0) {
+  const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  auto opt = weight.options();
+  at::Tensor g32 = grad_output.to(at::kFloat);
+  at::Tensor gm = g32;
+  if (activation) {
+    at::Tensor z = wide_pre_activation(x, bin_edges, inv_bin_widths, n_bins, weight, bias, epilogue, compute_dtype);
+    gm = g32.masked_fill(z <= 0, 0.0);  // threshold_backward: NaN inputs pass the gradient
+  }
+  at::Tensor gx = compute_grad_x ? at::empty_like(x) : at::empty({0}, x.options());
+  at::Tensor gw = compute_grad_weight ? at::empty_like(weight) : at::empty({0}, opt);
+  if (compute_grad_x || compute_grad_weight) {
+    at::Tensor gq = gm.to(compute_dtype).contiguous();
+    at::Tensor ws = workspace_for(x, N, F, B, D);
+    check_status(ple_backward(gq.data_ptr(), to_code(compute_dtype), x.data_ptr<float>(),
+                              bin_edges.data_ptr<float>(), inv_bin_widths.data_ptr<float>(),
+                              n_bins.data_ptr<int32_t>(), weight.data_ptr<float>(), nullptr, PLE_DTYPE_I32, N, F,
+                              B, D, compute_grad_x ? gx.data_ptr<float>() : nullptr,
+                              compute_grad_weight ? gw.data_ptr<float>() : nullptr, ws.data_ptr(),
+                              (size_t)ws.numel(), stream_of(x)),
+                 "rtdl_num_embeddings_cuda::embeddings_backward");
+  }
+  at::Tensor gb = want_bias ? gm.sum(0) : at::empty({0}, opt);
+  at::Tensor gw0 = want_l0 ? (g32 * x.unsqueeze(-1)).sum(0) : at::empty({0}, opt);
+  at::Tensor gb0 = want_l0 ? g32.sum(0) : at::empty({0}, opt);
+  if (compute_grad_x && epilogue == PLE_EPILOGUE_B) {
+    TORCH_CHECK(w0.has_value(), "epilogue B needs w0");
+    gx.add_((g32 * *w0).sum(-1));
+  }
+  return {gx, gw, gb.contiguous(), gw0.contiguous(), gb0.contiguous()};
+}
+
 at::Tensor ple_embeddings_forward_op(const at::Tensor& x, const at::Tensor& bin_edges,
                                      const at::Tensor& inv_bin_widths, const at::Tensor& n_bins,
                                      const at::Tensor& weight, const std::optional<at::Tensor>& bias,
@@ -201,6 +255,15 @@ at::Tensor ple_embeddings_forward_op(const at::Tensor& x, const at::Tensor& bin_
               "compute_dtype must be float32, float16, or bfloat16");
   c10::cuda::CUDAGuard guard(x.device());
   const int64_t N = x.size(0), F = x.size(1), B = weight.size(1), D = weight.size(2);
+  if (B > 256) {
+    at::Tensor z = wide_pre_activation(x, bin_edges, inv_bin_widths, n_bins, weight, bias, epilogue, compute_dtype);
+    at::Tensor y = activation ? at::relu(z) : z;
+    if (epilogue == PLE_EPILOGUE_B) {
+      TORCH_CHECK(w0.has_value() && b0.has_value(), "epilogue B needs w0 and b0");
+      y = at::addcmul(*b0, x.unsqueeze(-1), *w0) + y;
+    }
+    return y.to(output_dtype).contiguous();
+  }
   at::Tensor out = at::empty({N, F, D}, weight.options().dtype(output_dtype));
   if (out.numel() == 0) return out;
   // bin indices are not requested: the fused backward finds the bins itself, which costs less than
@@ -246,7 +309,10 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> ple_embed
   auto opt = weight.options();
   const bool want_bias = compute_grad_bias && epilogue == PLE_EPILOGUE_A;
   const bool want_l0 = compute_grad_linear0 && epilogue == PLE_EPILOGUE_B;
-  if (backward_needs_even_d(D) && N > 0 && (compute_grad_x || compute_grad_weight || want_bias || want_l0)) {
+  if (B > 256)
+    return wide_embeddings_backward(grad_output, x, bin_edges, inv_bin_widths, n_bins, weight, bias, w0, b0, epilogue,
+                                    activation, compute_dtype, compute_grad_x, compute_grad_weight, want_bias, want_l0);
+  if (backward_needs_even_d(B, D) && N > 0 && (compute_grad_x || compute_grad_weight || want_bias || want_l0)) {
     auto r = ple_embeddings_backward_op(pad_d(grad_output), x, bin_edges, inv_bin_widths, n_bins, pad_d(weight),
                                         pad_d(bias), pad_d(w0), pad_d(b0), bin_indices, epilogue, activation,
                                         compute_dtype, compute_grad_x, compute_grad_weight, compute_grad_bias,

@@ -58,13 +58,17 @@ int dtype_size(int dt) {
   }
 }
 
-int check_sizes(int64_t N, int64_t F, int64_t B, int64_t D) {
+// max_bins: 256 for the main kernels; the bare x_ple ops also take wider features (ple_wide.cu).
+int check_sizes(int64_t N, int64_t F, int64_t B, int64_t D, int64_t max_bins = 256) {
   if (N < 0) return set_error(PLE_ERR_SHAPE, "batch must be >= 0");
   if (F <= 0) return set_error(PLE_ERR_SHAPE, "n_features must be positive");
   if (B <= 0) return set_error(PLE_ERR_SHAPE, "max_n_bins must be positive");
   if (D <= 0) return set_error(PLE_ERR_SHAPE, "d_embedding must be positive");
   if (D > kMaxD) return set_error(PLE_ERR_UNSUPPORTED, "d_embedding must be <= 64");
-  if (B > 256) return set_error(PLE_ERR_UNSUPPORTED, "max_n_bins > 256 is not supported by the sm_100a kernels");
+  if (B > max_bins)
+    return set_error(PLE_ERR_UNSUPPORTED, B > kWideMaxBins ? "max_n_bins above 2^20 is not supported"
+                                                          : "max_n_bins > 256 needs the bare x_ple op (no epilogue, "
+                                                            "no activation)");
   if (F > (int64_t)1 << 30) return set_error(PLE_ERR_OVERFLOW, "n_features too large");
   if (N > 0 && F > INT64_MAX / N / D) return set_error(PLE_ERR_OVERFLOW, "N * F * D overflows int64");
   return PLE_OK;
@@ -156,7 +160,7 @@ static int forward_impl(const float* x, const float* edges, const float* inv_w, 
                         int relu, int compute_dtype, int64_t N, int64_t F, int64_t B, int64_t D,
                         int out_dtype, void* out, int bin_idx_dtype, void* bin_idx, void* stream) {
   g_msg[0] = 0;
-  int st = check_sizes(N, F, B, D);
+  int st = check_sizes(N, F, B, D, epi == kEpiNone && !relu ? kWideMaxBins : 256);
   if (st) return st;
   if ((st = check_tables(edges, inv_w, n_bins, W))) return st;
   if (dtype_size(out_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "output dtype must be F32, F16 or BF16");
@@ -180,6 +184,7 @@ static int forward_impl(const float* x, const float* edges, const float* inv_w, 
   a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.W = W;
   a.bias = bias; a.w0 = w0; a.b0 = b0; a.out = out; a.bin_idx = bin_idx; a.bin_idx_bytes = idx_bytes;
   a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D; a.epi = epi; a.relu = relu ? 1 : 0;
+  if (B > 256) return launch_forward_wide(a, compute_dtype, out_dtype, static_cast<cudaStream_t>(stream));
   const int vec = pick_vec(D, 4, {{out, dtype_size(out_dtype)}, {bias, 4}, {w0, 4}, {b0, 4}});
   return launch_forward(a, compute_dtype, out_dtype, vec, static_cast<cudaStream_t>(stream));
 }
@@ -205,7 +210,8 @@ int ple_embeddings_forward(const float* x, const float* bin_edges, const float* 
 
 size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t max_n_bins,
                                    int64_t d_embedding) {
-  if (check_sizes(batch, n_features, max_n_bins, d_embedding) != PLE_OK) return 0;
+  if (check_sizes(batch, n_features, max_n_bins, d_embedding, kWideMaxBins) != PLE_OK) return 0;
+  if (max_n_bins > 256) return wide_workspace_bytes(n_features, max_n_bins, d_embedding);
   size_t b = backward_workspace_bytes(batch < 1 ? 1 : batch, n_features, max_n_bins, d_embedding);
   return b ? b : 16;
 }
@@ -217,7 +223,7 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
                          float* grad_W, float* grad_bias, float* grad_w0, float* grad_b0, void* ws,
                          size_t ws_bytes, void* stream) {
   g_msg[0] = 0;
-  int st = check_sizes(N, F, B, D);
+  int st = check_sizes(N, F, B, D, epi == kEpiNone && !relu ? kWideMaxBins : 256);
   if (st) return st;
   if ((st = check_tables(edges, inv_w, n_bins, W))) return st;
   if (dtype_size(grad_dtype) == 0) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad dtype must be F32, F16 or BF16");
@@ -243,6 +249,15 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
   if (!g || !x) return set_error(PLE_ERR_INVALID_ARGUMENT, "grad_output and x are required");
   if (!ws) return set_error(PLE_ERR_WORKSPACE, "backward needs a workspace (ple_backward_workspace_size)");
   if (!aligned(ws, 16)) return set_error(PLE_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+  if (B > 256) {  // bare x_ple op over wide features: bins are recomputed, bin_indices are not read
+    if (!aligned(g, dtype_size(grad_dtype))) return set_error(PLE_ERR_ALIGNMENT, "grad_output is misaligned");
+    BwdArgs a{};
+    a.g = g; a.x = x; a.edges = edges; a.inv_w = inv_w; a.n_bins = n_bins; a.W = W;
+    a.grad_x = grad_x; a.grad_W = grad_W;
+    a.ws = static_cast<float*>(ws); a.ws_bytes = ws_bytes;
+    a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D; a.epi = kEpiNone;
+    return launch_backward_wide(a, compute_dtype, grad_dtype, s);
+  }
   const int vec = backward_vec(D, dtype_size(grad_dtype));
   if (D / vec > 32) return set_error(PLE_ERR_UNSUPPORTED, "backward: odd d_embedding above 32 is not supported");
   // widest power of two (<= 16 bytes) dividing a lane's chunk of grad_output / of an fp32 parameter row

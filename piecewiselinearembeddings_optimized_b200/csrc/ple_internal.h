@@ -107,6 +107,11 @@ int device_sm_count();
 size_t device_max_smem_optin();
 
 int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cudaStream_t st);
+// max_n_bins above 256 (bare x_ple ops only): global-memory kernels in ple_wide.cu
+constexpr int64_t kWideMaxBins = (int64_t)1 << 20;
+int launch_forward_wide(const FwdArgs& a, int compute_dtype, int output_dtype, cudaStream_t st);
+int launch_backward_wide(const BwdArgs& a, int compute_dtype, int grad_dtype, cudaStream_t st);
+size_t wide_workspace_bytes(int64_t F, int64_t B, int64_t D);
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);

@@ -158,8 +158,8 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
     memory; the result is bf16, as autocast's Linear returns.  With
     ``bf16_linear=True`` and no autocast the fp32 module output is rounded to
     bf16 for the product and the result is fp32.  Everything else (CPU inputs,
-    fp16 autocast, plain fp32, d_embedding not a multiple of 8) runs the
-    composition: the module's own kernel followed by ``linear``.
+    fp16 autocast, plain fp32, d_embedding not a multiple of 8, more than 256
+    bins) runs the composition: the module's own kernel followed by ``linear``.
 
     ``fused=False`` always runs the composition.  The trade-off: the fused
     kernel never allocates the ``[N, F, D]`` activation (805 MB at 65,536 rows
@@ -182,6 +182,8 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
 
     def _fused_dtypes(self, x: Tensor):
         if not self.fused or x.device.type != "cuda" or self.embeddings.d_embedding % 8 != 0:
+            return None
+        if self.embeddings.linear.weight.shape[1] > 256:  # the fused kernel's tables hold up to 256 bins
             return None
         if torch.is_autocast_enabled("cuda"):
             if torch.get_autocast_dtype("cuda") != torch.bfloat16:

@@ -49,13 +49,26 @@ FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails before an
     (4, 3, 4, 0, 2, "d_embedding"),
     (-1, 3, 4, 8, 2, "batch"),
     (4, 3, 4, 65, 4, "<= 64"),
-    (4, 3, 300, 8, 4, "max_n_bins"),
+    (4, 3, (1 << 20) + 1, 8, 4, "max_n_bins"),
 ])
 def test_forward_rejects_bad_sizes(n, f, b, d, code, msg):
     lib = _native.capi()
     st = lib.ple_forward(FAKE, FAKE, FAKE, FAKE, FAKE, n, f, b, d, 0, FAKE, 3, None, None)
     assert st == code
     assert msg in lib.ple_last_error_message().decode()
+
+
+def test_wide_bins_only_for_the_bare_op():
+    """More than 256 bins: the bare x_ple op runs its wide-bin kernels; an
+    epilogue or activation is refused before any launch."""
+    lib = _native.capi()
+    st = lib.ple_embeddings_forward(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 1, 0, 0,
+                                    4, 3, 300, 8, 0, FAKE, 3, None, None)
+    assert st == 4 and b"max_n_bins > 256" in lib.ple_last_error_message()
+    st = lib.ple_embeddings_forward(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 0, 1, 0,
+                                    4, 3, 300, 8, 0, FAKE, 3, None, None)
+    assert st == 4
+    assert lib.ple_backward_workspace_size(4, 3, 300, 8) == 2 * 3 * 300 * 8 * 4
 
 
 def test_forward_rejects_missing_tables_and_bad_dtypes():

@@ -149,6 +149,60 @@ def test_reference_backward_odd_wide_d(ops, cuda_device, d):
     assert gx2.numel() == 0 and torch.equal(gw2, gw)
 
 
+# more than 256 bins: int16 / int32 bin indices, the global-memory kernels of the bare x_ple op, and the
+# module's epilogue composed around it
+
+def _wide_bins(n_bins, seed):
+    rng = np.random.default_rng(seed)
+    return [(np.cumsum(rng.random(n + 1) + 0.01) - 0.3 * n).astype(np.float32) for n in n_bins]
+
+
+def _wide_x(bins, n, seed):
+    x = cases.sample_x(bins, n, seed)
+    x[:8, 0] = bins[0][10:18]  # exact interior edges: the boundary sub-gradient
+    return x
+
+
+@pytest.mark.parametrize("n_bins,idx_dtype", [((300, 5, 1, 120), torch.int16), ((40000, 3), torch.int32)])
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_reference_ops_wide_bins(ops, cuda_device, n_bins, idx_dtype, mode):
+    bins = _wide_bins(n_bins, 31)
+    d = 6
+    x = _wide_x(bins, 64, 32)
+    edges, inv_w, nb = o.pad_bins(bins)
+    w, *_ = cases.init_params(len(bins), edges.shape[1] - 1, d, "A", 33)
+    tx, te, tr, tn, tw = to_dev(cuda_device, x, edges, inv_w, nb, w)
+    xp, idx = ops.forward(tx, te, tr, tn, tw, TORCH_DT[mode])
+    assert idx.dtype == idx_dtype
+    ref_xp, ref_k = o.x_ple_forward(x, edges, inv_w, nb, w, mode)
+    np.testing.assert_array_equal(idx.cpu().numpy().astype(np.int64), ref_k)
+    np.testing.assert_allclose(xp.float().cpu().numpy(), ref_xp, **(FWD_TOL if mode == "f32" else LOW_TOL))
+    g = o.quantize(np.random.default_rng(34).standard_normal((64, len(bins), d)).astype(np.float32), mode)
+    tg = torch.from_numpy(g).to(cuda_device).to(TORCH_DT[mode])
+    gx, gw = ops.backward(tg, tx, te, tr, tn, tw, idx, True, True)
+    rgx, rgw, rabs = o.x_ple_backward(g, x, edges, inv_w, nb, w, mode, with_abs=True)
+    tol = GRAD_TOL if mode == "f32" else LOW_GRAD_TOL
+    np.testing.assert_allclose(gx.cpu().numpy(), rgx, **tol)
+    o.assert_reduction_close(gw.cpu().numpy(), rgw, rabs, err_msg="grad_W", **tol)
+    gx2, gw2 = ops.backward(tg, tx, te, tr, tn, tw, idx, True, False)
+    assert gw2.numel() == 0 and torch.equal(gx2, gx)
+
+
+@pytest.mark.parametrize("version", ["A", "B"])
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("mode,out_mode", [("f32", "f32"), ("bf16", "f32"), ("bf16", "bf16")])
+def test_fused_wide_bins_match_oracle(ops, cuda_device, version, relu, mode, out_mode):
+    bins = _wide_bins((260, 7, 2, 512), 41)
+    d = 10
+    x = _wide_x(bins, 96, 42)
+    edges, inv_w, nb = o.pad_bins(bins)
+    w, bias, w0, b0 = cases.init_params(len(bins), edges.shape[1] - 1, d, version, 43)
+    g = o.quantize(np.random.default_rng(44).standard_normal((96, len(bins), d)).astype(np.float32), out_mode)
+    res = run_fused(ops, cuda_device, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, mode, out_mode,
+                    reuse_bins=relu)
+    compare_fused(res, x, edges, inv_w, nb, w, bias, w0, b0, g, version, relu, mode, out_mode)
+
+
 # ---------------------------------------------------------------- reference-interface ops
 
 @pytest.mark.parametrize("case", cases.BIN_CASES)
