@@ -106,10 +106,24 @@ def test_fake_tensor_shapes():
 @pytest.mark.parametrize("activation", [False, True])
 @pytest.mark.parametrize("case", ["equal", "ragged", "single_bin", "all_single_bin", "ties"])
 def test_module_autograd_matches_oracle(cuda_device, version, activation, case):
-    bins = _bins(case)
+    _check_module_autograd(cuda_device, _bins(case), version, activation, integer=(case == "ties"))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("version", ["A", "B"])
+@pytest.mark.parametrize("activation", [False, True])
+def test_module_autograd_more_than_256_bins(cuda_device, version, activation):
+    """300 bins in one feature: int16 bin indices and the wide-bin kernels, through the module and autograd."""
+    rng = np.random.default_rng(17)
+    bins = [torch.from_numpy((np.cumsum(rng.random(n + 1) + 0.01) - 0.3 * n).astype(np.float32))
+            for n in (300, 4, 1, 57)]
+    _check_module_autograd(cuda_device, bins, version, activation)
+
+
+def _check_module_autograd(cuda_device, bins, version, activation, integer=False):
     m = rnc.CudaPiecewiseLinearEmbeddings(bins, 16, activation=activation, version=version).to(cuda_device)
     _init(m, 3)
-    xn = cases.sample_x([b.numpy() for b in bins], 128, 5, integer=(case == "ties"))
+    xn = cases.sample_x([b.numpy() for b in bins], 128, 5, integer=integer)
     x = torch.from_numpy(xn).to(cuda_device).requires_grad_(True)
     y = m(x)
     assert y.dtype == torch.float32 and y.shape == (128, len(bins), 16)
