@@ -235,3 +235,23 @@ def test_module_bf16_linear_fp32_and_fallbacks(cuda_device):
         assert torch.equal(fused(x), composed)
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         assert torch.equal(fused(x), lin(emb(x).flatten(1)))
+
+
+@pytest.mark.gpu
+def test_module_more_than_256_bins_runs_the_composition(cuda_device):
+    """The fused kernel's tables hold up to 256 bins; wider modules run the composition (bit-equal)."""
+    import rtdl_num_embeddings_cuda as rc
+
+    torch.manual_seed(4)
+    rng = np.random.default_rng(4)
+    bins = [torch.from_numpy((np.cumsum(rng.random(n + 1) + 0.01) - 0.3 * n).astype(np.float32))
+            for n in (300, 9, 64)]
+    emb = rc.CudaPiecewiseLinearEmbeddings([b.to(cuda_device) for b in bins], 16, activation=True,
+                                           version="A").to(cuda_device)
+    lin = torch.nn.Linear(len(bins) * 16, 32).to(cuda_device)
+    fused = rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin)
+    x = torch.randn(64, len(bins), device=cuda_device) * 40
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        z = fused(x)
+        assert z.dtype == torch.bfloat16
+        assert torch.equal(z, lin(emb(x).flatten(1)))
