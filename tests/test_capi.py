@@ -68,7 +68,13 @@ def test_wide_bins_only_for_the_bare_op():
     st = lib.ple_embeddings_forward(FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 0, 1, 0,
                                     4, 3, 300, 8, 0, FAKE, 3, None, None)
     assert st == 4
+    # grad_output, dtype, x, edges, inv_w, n_bins, W, bias, w0, b0, epilogue A, relu, compute, N, F, B, D,
+    # bin_indices, dtype, grad_x, grad_W, grad_bias, grad_w0, grad_b0, workspace, bytes, stream
+    st = lib.ple_embeddings_backward(FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 1, 1, 0,
+                                     4, 3, 300, 8, None, 0, FAKE, FAKE, FAKE, None, None, FAKE, 1 << 20, None)
+    assert st == 4 and b"max_n_bins > 256" in lib.ple_last_error_message()
     assert lib.ple_backward_workspace_size(4, 3, 300, 8) == 2 * 3 * 300 * 8 * 4
+    assert lib.ple_backward_workspace_size(4, 3, (1 << 20) + 1, 8) == 0
 
 
 def test_forward_rejects_missing_tables_and_bad_dtypes():
