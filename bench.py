@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override the global batch (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c4", action="store_true", help="skip the c4 north-star figures of the default run")
     ap.add_argument("--consumer", type=int, default=None, metavar="H",
                     help="time the module fused into a following Linear(F*D -> H) (forward, bf16 autocast "
                          "semantics) against the unfused embeddings kernel + cuBLAS, one GPU")
@@ -258,6 +259,77 @@ def consumer_bench(args) -> int:
     }
     print(json.dumps(line))
     return 0 if status == 0 else 1
+
+
+def north_star_c4(torch, dev, lib, steps, warmup, peak):
+    """The north-star target shape timed beside the headline workload (one GPU): configuration c4
+    (65,536 x 256, 32 bins, D = 24, bf16 output and upstream gradient, version B + ReLU), one step =
+    the fused forward then the fused backward (kernel + finalize) with every input resident in HBM,
+    CUDA events on the compute stream.  Target: >= 70 % of the HBM roofline, i.e. a step of at most
+    324 us at 8 TB/s, 401 us at the measured copy bandwidth."""
+    from piecewiselinearembeddings_optimized_b200 import _native, workloads
+    from piecewiselinearembeddings_optimized_b200.module import pad_bin_tables
+
+    n0, F, D, version, relu, mode, out_mode = workloads.SPECS["c4"]
+    wl = workloads.make_workload("c4", n=8)
+    B = wl.max_n_bins
+    edges, inv_w, n_bins = [t.to(dev) for t in pad_bin_tables([torch.from_numpy(b) for b in wl.bins])]
+    W = torch.from_numpy(wl.weight).to(dev)
+    w0, b0 = torch.from_numpy(wl.w0).to(dev), torch.from_numpy(wl.b0).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(4000)
+    x = torch.randn(n0, F, device=dev, generator=gen)
+    m = torch.rand(n0, F, device=dev, generator=gen) < 0.01
+    x[m] = torch.where(torch.rand(n0, F, device=dev, generator=gen) < 0.5, -10.0, 10.0)[m]
+    g = torch.randn(n0, F, D, device=dev, generator=gen).to(torch.bfloat16)
+    y = torch.empty(n0, F, D, device=dev, dtype=torch.bfloat16)
+    gx = torch.empty(n0, F, device=dev)
+    gW = torch.empty(F, B, D, device=dev)
+    gw0, gb0 = torch.empty(F, D, device=dev), torch.empty(F, D, device=dev)
+    ws_bytes = lib.ple_backward_workspace_size(n0, F, B, D)
+    wsp = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    bf = _native.DTYPE_BF16
+
+    def fwd():
+        _native.check(lib.ple_embeddings_forward(
+            x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(), W.data_ptr(), None, w0.data_ptr(),
+            b0.data_ptr(), 2, 1, bf, n0, F, B, D, bf, y.data_ptr(), 3, None, sp), "c4 forward")
+
+    def bwd():
+        _native.check(lib.ple_embeddings_backward(
+            g.data_ptr(), bf, x.data_ptr(), edges.data_ptr(), inv_w.data_ptr(), n_bins.data_ptr(), W.data_ptr(), None,
+            w0.data_ptr(), b0.data_ptr(), 2, 1, bf, n0, F, B, D, None, 3, gx.data_ptr(), gW.data_ptr(), None,
+            gw0.data_ptr(), gb0.data_ptr(), wsp.data_ptr(), ws_bytes, sp), "c4 backward")
+
+    for _ in range(max(3, warmup)):
+        fwd()
+        bwd()
+    torch.cuda.synchronize(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for k in range(steps):
+        ev[k][0].record()
+        fwd()
+        ev[k][1].record()
+        bwd()
+        ev[k][2].record()
+    torch.cuda.synchronize(dev)
+    fwd_ms = float(np.median([e[0].elapsed_time(e[1]) for e in ev]))
+    bwd_ms = float(np.median([e[1].elapsed_time(e[2]) for e in ev]))
+    step_ms = float(np.median([e[0].elapsed_time(e[2]) for e in ev]))
+    wb = workloads.algorithmic_bytes(wl, n_local=n0)
+    step_gbs = wb["step"] / (step_ms * 1e-3) / 1e9
+    return {
+        "workload": "c4: 65536 x 256 features, 32 bins, D=24, bf16 output and gradient, version B + ReLU",
+        "ms_per_step": step_ms, "us_per_step": step_ms * 1e3, "target_us_8tbs": wb["step"] / 8000e9 / 0.7 * 1e6,
+        "target_us_measured_peak": wb["step"] / (peak * 1e9) / 0.7 * 1e6,
+        "feature_embeddings_per_s": n0 * F / (step_ms * 1e-3), "step_gb_per_s": step_gbs,
+        "step_frac_of_measured": step_gbs / peak, "step_frac_of_8tbs": step_gbs / 8000.0,
+        "kernels": {"forward": {"ms": fwd_ms, "gb_per_s": wb["fwd"] / (fwd_ms * 1e-3) / 1e9,
+                                "frac": wb["fwd"] / (fwd_ms * 1e-3) / 1e9 / peak},
+                    "backward": {"ms": bwd_ms, "gb_per_s": wb["bwd"] / (bwd_ms * 1e-3) / 1e9,
+                                 "frac": wb["bwd"] / (bwd_ms * 1e-3) / 1e9 / peak}},
+        "timing": f"median of {steps} steps after {max(3, warmup)} warm-up steps, CUDA events; inputs resident in HBM",
+    }
 
 
 def config_block(name, n_global, ws):
@@ -478,7 +550,7 @@ def main() -> int:
         "backward": {"ms": bwd_ms, "bytes": wl_bytes["bwd"], "gbs": wl_bytes["bwd"] / (bwd_ms * 1e-3) / 1e9},
     }
     dom = max(kernels, key=lambda k: kernels[k]["ms"])
-    traffic = read_traffic(name, dom)
+    traffic = read_traffic(name, dom, n_local)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": kernels[dom]["gbs"] / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                 if peak_kind == "measured" else "fallback 6650 GB/s",
@@ -495,6 +567,8 @@ def main() -> int:
         "allreduce_ms": ar_ms, "roofline": roofline, "clocks": clk,
         "gpu_launches": 3 * args.steps, "e2e": e2e,
     }
+    if ws == 1 and name == "c5" and not args.no_c4:
+        line["north_star_c4"] = north_star_c4(torch, dev, lib, max(10, args.steps), args.warmup, peak)
     if ws == 1 and not args.no_cpu_baseline:
         from oracle.cpu_baseline import time_cpu_baseline
 
@@ -507,17 +581,19 @@ def main() -> int:
     return 0
 
 
-def read_traffic(config: str, kernel: str):
-    """DRAM bytes per launch from a committed ncu summary, if one exists
-    (``profiles/traffic.txt`` lines: ``<config> <kernel> <bytes_per_launch> <note>``)."""
+def read_traffic(config: str, kernel: str, n_local: int):
+    """DRAM bytes of one launch over ``n_local`` rows, from a committed ncu summary if one exists
+    (``profiles/traffic.txt`` lines: ``<config> <kernel> <bytes_per_launch> <rows> <note>``, the bytes of a
+    launch over ``rows`` rows; every term of the traffic but the small tables grows with the rows, so the
+    figure is scaled to the rows this rank's launch processes)."""
     p = ROOT / "profiles" / "traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
         parts = line.split()
-        if len(parts) >= 3 and parts[0] == config and parts[1] == kernel:
+        if len(parts) >= 4 and parts[0] == config and parts[1] == kernel:
             try:
-                return float(parts[2])
+                return float(parts[2]) * n_local / float(parts[3])
             except ValueError:
                 return None
     return None

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 5
+#define PLE_ABI_VERSION 6
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -79,24 +79,14 @@ int ple_abi_version(void);
 const char* ple_status_string(int status);
 
 /*
- * Backward kernels.  ple_backward and ple_embeddings_backward run the sorted
- * kernel (a per-tile counting sort by bin and a segmented walk).  With the
- * environment variable PLE_BACKWARD_KERNEL=tensor they run the tensor-core
- * kernel instead (per-bin sums as one-hot GEMMs on tcgen05, exact bf16 part
- * splits, TMEM accumulators), which covers max_n_bins <= 128, d_embedding a
- * multiple of 8 up to 32 and the shapes whose tiles fit, and returns
- * PLE_ERR_UNSUPPORTED elsewhere.  Both are deterministic and give the same
- * results within the fp32 summation tolerance; the sorted kernel is the faster
- * one on the measured configurations.
- *
- * Status word of the tensor-core backward on the current device: 1 if one of
- * its waits for the tensor core ran past its iteration limit since the last
- * call (that launch then skipped its remaining work, so its gradients are
- * incomplete, and released its tensor memory), 0 if not, -1 if the word could
- * not be read.  Reading clears it.  Synchronous (a device-to-host copy).
- * No counterpart in the reference.
+ * Backward kernel.  ple_backward and ple_embeddings_backward (and the
+ * no-allocation variant) run one kernel: per tile of samples a counting sort
+ * of each feature's samples by bin, then a segmented walk over the sorted
+ * lists that keeps each run's gradient sums in registers; the parameter
+ * gradients are summed per partition in the workspace and reduced in a fixed
+ * order, so every result is bitwise deterministic for a given shape and
+ * device.
  */
-int ple_tensor_core_status(void);
 
 /* Detail message of the last failing call on the calling host thread. */
 const char* ple_last_error_message(void);
@@ -193,16 +183,20 @@ int ple_embeddings_backward(const void* grad_output, int grad_dtype, const float
  * call: the scratch is a static device array of PLE_NOALLOC_SCRATCH_BYTES
  * (16 MiB) per device, placed when the library's module is loaded.
  *
- *   - Same arguments, results and status codes as ple_embeddings_backward,
- *     without workspace / workspace_bytes.
+ *   - Same arguments, results, size limits and status codes as
+ *     ple_embeddings_backward, without workspace / workspace_bytes (more
+ *     than 256 bins only for the bare x_ple case: no epilogue, no
+ *     activation).
  *   - Sizes whose workspace (ple_backward_workspace_size) exceeds
  *     PLE_NOALLOC_SCRATCH_BYTES are rejected with PLE_ERR_WORKSPACE before
  *     anything is launched; use ple_embeddings_backward for those.
  *   - The scratch does not need to start at zero: every slot that the
- *     finalize step reads is written earlier in the same call.
+ *     finalize step reads is written earlier in the same call (the
+ *     wide-bin path clears what it accumulates into with cudaMemsetAsync).
  *   - The first call on each device looks up the scratch address
- *     (cudaGetSymbolAddress, once per device); make that first call before
- *     any stream capture on the device.
+ *     (cudaGetSymbolAddress, with that device current) and caches it; a
+ *     lookup that fails is not cached and the next call tries again.  Make
+ *     the first call before any stream capture on the device.
  *   - One scratch per device, shared by all calls: two calls whose kernels
  *     can overlap on the same device (different streams, or host threads
  *     without ordering) race on it and corrupt each other's results.  Order
@@ -300,10 +294,10 @@ int ple_embeddings_linear_forward(const float* x, const float* bin_edges, const 
                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Status word of ple_embeddings_linear_forward on the current device, as
- * ple_tensor_core_status: 1 if a wait of the kernel ran past its iteration
- * limit since the last call (that launch's output is incomplete), 0 if not,
- * -1 if unreadable.  Reading clears it.
+ * Status word of ple_embeddings_linear_forward on the current device: 1 if a
+ * wait of the kernel ran past its iteration limit since the last call (that
+ * launch's output is incomplete), 0 if not, -1 if unreadable.  Reading clears
+ * it.  Synchronous (a device-to-host copy).
  */
 int ple_linear_status(void);
 

@@ -55,8 +55,6 @@ def capi() -> ctypes.CDLL:
     P, I64, I, SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
     lib.ple_abi_version.restype = I
     lib.ple_abi_version.argtypes = []
-    lib.ple_tensor_core_status.restype = I
-    lib.ple_tensor_core_status.argtypes = []
     lib.ple_status_string.restype = ctypes.c_char_p
     lib.ple_status_string.argtypes = [I]
     lib.ple_last_error_message.restype = ctypes.c_char_p

@@ -1,17 +1,23 @@
 // ple_backward.cu - planning, workspace and finalize of the fused PLE backward
 // (the kernel itself is in ple_backward_impl.cuh, instantiated per dtype pair
 // in ple_backward_<dtypes>.cu so that the instantiations compile in parallel).
+//
+// Workspace: one partial [Fc][B + 3][D] fp32 block per (slot, segment of the
+// slot's range, member CTA of the slot); rows 0..B-1 grad_W in the physical
+// layout, B the bias, B + 1 w0, B + 2 b0.  The finalize kernel sums, per
+// feature, the blocks of the slots whose ranges cover the feature's group,
+// in slot order (deterministic).
 #include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 
-#include "ple_backward_tc.cuh"
+#include <cudaTypedefs.h>
+
+#include "ple_backward_impl.cuh"
 
 namespace ple {
-
-// Set to 1 by a tensor-core backward whose wait expired (ple_tensor_core_status reads and clears it).
-__device__ int g_tc_dev_err = 0;
 
 int launch_bwd_f32(const BwdArgs& a, int vec, cudaStream_t st);
 int launch_bwd_bf16(const BwdArgs& a, int vec, cudaStream_t st);
@@ -19,14 +25,11 @@ int launch_bwd_bf16_f32(const BwdArgs& a, int vec, cudaStream_t st);
 int launch_bwd_f16(const BwdArgs& a, int vec, cudaStream_t st);
 int launch_bwd_f16_f32(const BwdArgs& a, int vec, cudaStream_t st);
 
-// Sum, per feature, the partials of the CTAs whose ranges cover its chunk, in
-// CTA order (deterministic).  Rows whose gradient was not requested are
-// neither read nor written.
-__global__ void ple_bwd_finalize_kernel(const BwdArgs a, int grid) {
-  const int B = a.B, D = a.D, Fc = a.Fc;
+__global__ void ple_bwd_finalize_kernel(const BwdArgs a, int n_slots) {
+  const int B = a.B, D = a.D, Fc = a.Fc, m = a.group;
   const int64_t rows = (int64_t)a.F * (B + 3) * D;
-  const int64_t total = (int64_t)a.n_chunks * a.N;
-  const int64_t slot = (int64_t)Fc * (B + 3) * D;
+  const int64_t total = (int64_t)a.n_groups * a.N;
+  const int64_t block = (int64_t)Fc * (B + 3) * D;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t f = idx / ((int64_t)(B + 3) * D);
@@ -38,19 +41,20 @@ __global__ void ple_bwd_finalize_kernel(const BwdArgs a, int grid) {
                               : (a.grad_b0 ? a.grad_b0 + f * D + d : nullptr);
     if (dst == nullptr) continue;
     const int chunk = (int)(f / Fc), i = (int)(f - (int64_t)chunk * Fc);
-    const int64_t c_lo = (int64_t)chunk * a.N, c_hi = c_lo + a.N;
-    // first CTA whose range [total*j/grid, total*(j+1)/grid) ends past the chunk start
-    int64_t j = c_lo * grid / total;
-    while (j > 0 && total * j / grid > c_lo) --j;
-    while (j < grid && total * (j + 1) / grid <= c_lo) ++j;
+    const int grp = chunk / m, member = chunk - grp * m;
+    const int64_t c_lo = (int64_t)grp * a.N, c_hi = c_lo + a.N;
+    // first slot whose range [total*j/n_slots, total*(j+1)/n_slots) ends past the group start
+    int64_t j = c_lo * n_slots / total;
+    while (j > 0 && total * j / n_slots > c_lo) --j;
+    while (j < n_slots && total * (j + 1) / n_slots <= c_lo) ++j;
     float s = 0.f;
-    for (; j < grid; ++j) {
-      const int64_t lo = total * j / grid;
-      const int64_t hi = total * (j + 1) / grid;
+    for (; j < n_slots; ++j) {
+      const int64_t lo = total * j / n_slots;
+      const int64_t hi = total * (j + 1) / n_slots;
       if (lo >= c_hi) break;
       if (hi <= lo) continue;
-      const int seg = chunk - (int)(lo / a.N);  // segments of CTA j are consecutive chunks
-      s += a.ws[(j * a.max_segs + seg) * slot + (int64_t)i * (B + 3) * D + rem];
+      const int seg = grp - (int)(lo / a.N);  // segments of slot j are consecutive groups
+      s += a.ws[((j * a.max_segs + seg) * m + member) * block + (int64_t)i * (B + 3) * D + rem];
     }
     *dst = s;
   }
@@ -65,21 +69,18 @@ int backward_vec(int64_t D, int /*grad_bytes*/) {
   return 1;
 }
 
-// Features per CTA (power of two) and tile length: the largest tile in
-// (feature, sample) pairs whose layout fits, preferring more features; false
-// if even one feature does not fit.
+// Features per CTA (power of two, up to 4) and tile length: the largest tile in (feature, sample) pairs
+// whose layout fits, preferring more features (wider gradient rows per sample for DRAM: measured, one
+// feature per CTA with 4096-sample tiles read 114 bytes of DRAM per 68-byte pair at c5 and ran 30%
+// slower than four features with 1024-sample tiles).  False if even one feature does not fit.
 static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
   const int nc = a.D / vec;
   if (nc > 32) return false;
-  int pow2 = 1;
-  while (pow2 < a.B + 1) pow2 <<= 1;
-  a.pow2 = pow2;
   a.lgk = 0;
   while ((1 << a.lgk) < a.B) ++a.lgk;
   const size_t optin = device_max_smem_optin();
-  constexpr int kWarps = kBwdThreads / 32;
   int lgWarps = 0;
-  while ((1 << lgWarps) < kWarps) ++lgWarps;
+  while ((1 << lgWarps) < kBwdWarps) ++lgWarps;
   int best = -1;
   for (int lgFc = 2; lgFc >= 0; --lgFc) {
     if (lgFc > lgWarps) continue;
@@ -87,10 +88,11 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
     const int Fc = 1 << lgFc;
     const int lgWf = lgWarps - lgFc;
     const int G = (1 << lgWf) * (32 / nc);
-    for (int lgSt = 12; lgSt >= 7; --lgSt) {
-      if (lgSt < lgWf) break;
-      BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G, nc};
-      const size_t bytes = bwd_layout_bytes(a.B, a.D, 1 << a.lgk, m, nullptr, nullptr);
+    for (int lgSt = 11; lgSt >= 7; --lgSt) {
+      if (lgSt < lgWf + 5) break;    // every warp ranks at least 32 samples of its quarter
+      if (lgSt - lgWf > 11) continue;  // ranks within a quarter take 11 bits of the entry
+      BwdDims m{Fc, 1 << lgWf, 1 << lgSt, G, nc, 1 << a.lgk};
+      const size_t bytes = bwd_layout_bytes(a.B, a.D, m, nullptr, nullptr);
       if (bytes > optin) continue;
       const int score = lgFc + lgSt;
       if (score > best) {
@@ -108,19 +110,27 @@ static bool bwd_plan(BwdArgs& a, int vec, size_t* smem_out) {
   return best >= 0;
 }
 
+// Slots of `group` CTAs: the CTAs of a slot cover consecutive chunks whose x / grad_x rows together fill
+// 64 bytes, over the same samples, so that the pieces of a row the members read and write meet in L2
+// (measured: 32-byte groups left about 13 bytes per pair of extra DRAM reads at c5).
 static void bwd_grid(BwdArgs& a, int* grid) {
-  const int64_t total = (int64_t)a.n_chunks * a.N;
-  int64_t g = device_sm_count();
-  const int64_t min_units = 64;  // at least 64 (chunk, sample) rows per CTA
-  if (g > total / min_units) g = total / min_units;
-  if (g < 1) g = 1;
-  *grid = (int)g;
-  const int64_t len = ceil_div<int64_t>(total, g);
-  a.max_segs = (int)(ceil_div<int64_t>(len, a.N) + 1);  // chunks one range can touch
+  int m = 64 / (4 * a.Fc);
+  if (m < 1) m = 1;
+  if (m > a.n_chunks) m = a.n_chunks;
+  a.group = m;
+  a.n_groups = (int)ceil_div<int64_t>(a.n_chunks, m);
+  const int64_t total = (int64_t)a.n_groups * a.N;
+  int64_t slots = device_sm_count() / m;
+  const int64_t min_units = 64;  // at least 64 (group, sample) rows per slot
+  if (slots > total / min_units) slots = total / min_units;
+  if (slots < 1) slots = 1;
+  *grid = (int)(slots * m);
+  const int64_t len = ceil_div<int64_t>(total, slots);
+  a.max_segs = (int)(ceil_div<int64_t>(len, a.N) + 1);  // groups one range can touch
 }
 
 static size_t ws_bytes_for(const BwdArgs& a, int grid) {
-  return (size_t)grid * a.max_segs * ((size_t)(1 << a.lgFc) * (a.B + 3) * a.D) * sizeof(float);
+  return (size_t)grid * a.max_segs * ((size_t)a.Fc * (a.B + 3) * a.D) * sizeof(float);
 }
 
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
@@ -130,176 +140,64 @@ size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
   if (!bwd_plan(b, backward_vec(D, 4), &smem)) return 0;
   int grid = 0;
   bwd_grid(b, &grid);
-  size_t bytes = ws_bytes_for(b, grid);
-  // the tensor-core kernel's needs for each compute type (parts of q(g') and of q(t) q(g'))
-  // (bf16 parts of H, of U, register cap) per (compute, gradient) type pair
-  const int parts[5][3] = {{3, 3, tc_max_regs<float>()}, {1, 2, tc_max_regs<__nv_bfloat16>()},
-                           {1, 2, tc_max_regs<float>()}, {2, 3, tc_max_regs<__half>()}, {2, 3, tc_max_regs<float>()}};
-  for (const auto& pp : parts) {
-    BwdArgs t{};
-    t.N = N; t.F = (int)F; t.B = (int)B; t.D = (int)D;
-    TcGeom m{};
-    int threads = 0, tg = 0;
-    if (tc_plan(t, pp[0], pp[1], tc_max_warps(pp[2]), &m, &threads, &smem)) bytes = std::max(bytes, tc_ws_floats(t, m, threads, &tg) * 4);
-  }
-  return bytes;
+  return ws_bytes_for(b, grid);
 }
 
 int bwd_prepare(BwdArgs& a, int vec, size_t* smem, int* grid) {
   if (!bwd_plan(a, vec, smem)) return set_error(PLE_ERR_UNSUPPORTED, "backward: tables do not fit in shared memory");
+  // sample offsets inside a tile are 32-bit: (tile length) * F * D elements must fit
+  if ((int64_t)(1 << a.lgSt) * a.F * a.D >= ((int64_t)1 << 32))
+    return set_error(PLE_ERR_UNSUPPORTED, "backward: n_features * d_embedding too large");
   bwd_grid(a, grid);
   if (ws_bytes_for(a, *grid) > a.ws_bytes)
     return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
-  a.x_vec4 = ((1 << a.lgFc) >= 4) && (a.F % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
   return PLE_OK;
 }
 
-// ------------------------------------------------------------ tensor-core kernel planning
-static int pow2_at_least(int v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
-
-static size_t tc_layout(TcGeom& m, int B, int D, int pow2) {
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    const size_t o = off;
-    off += (bytes + 127) & ~(size_t)127;
-    return (int)o;
-  };
-  const int units = m.nG * m.nh;
-  m.oA = take((size_t)2 * m.nG * 128 * m.R * 2);
-  m.oB = take((size_t)2 * m.nG * m.R * m.cols * 2);  // directly after A (zeroed together)
-  m.oT = take((size_t)B * m.ts * 4);
-  m.oS = take((size_t)B * m.ts * 4);
-  m.oE = take((size_t)pow2 * m.Fc * 4);
-  m.oR = take((size_t)B * m.Fc * 4);
-  m.oN = take((size_t)m.Fc * 4);
-  m.oGX = take((size_t)2 * m.R * m.Fc * m.nh * 4);  // [2][Fc * nh][R]
-  m.oTot = take((size_t)units * 4 * 8 * 4);
-  m.oKey = take((size_t)2 * m.R * m.Fc);
-  m.oBar = take(64);  // full[2], empty[2], TMEM address, non-finite flag, abort flag
-  (void)D;
-  return off;
-}
-
-// Geometry of the tensor-core kernel, false where it does not apply: bins <= 128 (padded to Bp = 32,
-// 64 or 128; FM = 128 / Bp features share an MMA's M = 128 rows), D a multiple of 8 up to 32 (one
-// warp of flush lanes per 8-column block and group), one feature's parts * D columns <= 256 (one MMA).
-bool tc_plan(const BwdArgs& a, int parts_h, int parts_u, int max_warps, TcGeom* m, int* threads, size_t* smem) {
-  const int B = a.B, D = a.D;
-  if (B < 1 || B > 128 || D % 8 != 0 || D > 32 || a.F < 1) return false;
-  int Bp = 32;
-  while (Bp < B) Bp <<= 1;
-  const int Cf = (parts_h + parts_u) * D;
-  if (Cf > 256) return false;
-  const int nh = D / 8;
-  const int pow2 = pow2_at_least(B + 1);
-  int lgp = 0;
-  while ((1 << lgp) < pow2) ++lgp;
-  const size_t optin = device_max_smem_optin();
-  // FM features stacked in the M = 128 rows (up to 128 / Bp; rows past FM * Bp stay zero), nG groups of
-  // accumulators plus 16 running-sum columns per unit (group, column block) in TMEM: the most of both whose
-  // producer warps and shared memory fit
-  for (int FM = 128 / Bp; FM >= 1; FM >>= 1) {
-    int fpm = FM;
-    while (fpm > 1 && fpm * Cf > 256) fpm >>= 1;
-    const int Nmma = (fpm * Cf + 15) & ~15;
-    const int n_mma = FM / fpm, cols = n_mma * Nmma;
-    int nG = kTcTmemCols / (cols + 16 * nh);
-    nG = std::min<int>(nG, (int)ceil_div<int64_t>(a.F, FM));
-    for (; nG >= 1; --nG) {
-      TcGeom g{};
-      g.Bp = Bp; g.FM = FM; g.fpm = fpm; g.Nmma = Nmma; g.n_mma = n_mma; g.cols = cols; g.nG = nG; g.nh = nh;
-      g.Fc = nG * FM;
-      g.ts = table_stride(g.Fc, D);
-      g.lgp = lgp;
-      // producer warps: a multiple of the (feature, column block) count C (each warp keeps one) and of 4
-      // (the TMEM lane quarters); each warp drains nu of the nG * nh units
-      const int C = g.Fc * nh;
-      int WP = C;
-      while (WP % 4) WP += C;
-      if (WP * 32 > kTcMaxProducers || WP + 1 > max_warps || (4 * nG * nh) % WP != 0) continue;
-      g.nu = 4 * nG * nh / WP;
-      g.R = 32 * kTcItems * WP / C;
-      size_t bytes = tc_layout(g, B, D, pow2);
-      // more than half of an SM's shared memory: one CTA per SM, so the 512-column TMEM allocation never waits
-      bytes = std::max<size_t>(bytes, 116 * 1024);
-      if (bytes > optin) continue;
-      g.flush_tiles = std::max(1, 256 / g.R);  // the accumulators are drained every 256 samples
-      *m = g;
-      *threads = 32 * WP;
-      *smem = bytes;
-      return true;
-    }
-  }
-  return false;
-}
-
-// Workspace floats of the tensor-core kernel: partials [grid][max_segs][Fc][B + 3][D], non-finite sums
-// [grid][Fc][Bp][2][D], epilogue scratch [grid][threads][16]; fills a's chunking and m's offsets.
-size_t tc_ws_floats(BwdArgs& a, TcGeom& m, int threads, int* grid) {
-  a.Fc = m.Fc;
-  a.n_chunks = (int)ceil_div<int64_t>(a.F, m.Fc);
-  const int64_t total = (int64_t)a.n_chunks * a.N;
-  int64_t g = device_sm_count();
-  const int64_t min_units = 64;
-  if (g > total / min_units) g = total / min_units;
-  if (g < 1) g = 1;
-  *grid = (int)g;
-  const int64_t len = ceil_div<int64_t>(total, g);
-  a.max_segs = (int)(ceil_div<int64_t>(len, a.N) + 1);
-  const int64_t partials = g * a.max_segs * (int64_t)m.Fc * (a.B + 3) * a.D;
-  m.spec_off = (partials + 63) & ~(int64_t)63;
-  const int64_t spec = g * (int64_t)m.Fc * m.Bp * 2 * a.D;
-  m.escr_off = (m.spec_off + spec + 63) & ~(int64_t)63;
-  return (size_t)(m.escr_off + g * (int64_t)threads * 16);
-}
-
-static int* tc_err_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  static int* cache[64] = {};
-  if (dev < 0 || dev >= 64) return nullptr;
-  if (!cache[dev]) {
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_tc_dev_err) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool bwd_grad_map(const BwdArgs& a, int elem, CUtensorMap* map) {
+  memset(map, 0, sizeof(*map));
+  const int gbytes = elem == 0 ? 4 : 2;
+  const int64_t cols = (int64_t)a.F * a.D;
+  const int box_cols = a.Fc * a.D;
+  if (a.N < 1 || a.N > 0x7fffffff || cols > 0x7fffffff) return false;
+  if (box_cols > 256 || (box_cols * gbytes) % 16 != 0 || (cols * gbytes) % 16 != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(a.g) & 15) != 0) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const CUtensorMapDataType dt = elem == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                               : elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)a.N};
+  const cuuint64_t strides[1] = {(cuuint64_t)(cols * gbytes)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, 256u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = enc(map, dt, 2, const_cast<void*>(a.g), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    memset(map, 0, sizeof(*map));
+    return false;
   }
-  return cache[dev];
-}
-
-int tc_prepare(BwdArgs& a, TcGeom& m, int threads, int* grid) {
-  a.pow2 = pow2_at_least(a.B + 1);
-  const size_t floats = tc_ws_floats(a, m, threads, grid);
-  if (floats * 4 > a.ws_bytes)
-    return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
-  m.dev_err = tc_err_ptr();
-  if (!m.dev_err) return set_error(PLE_ERR_CUDA, "tensor-core backward: status word not addressable");
-  return PLE_OK;
-}
-
-int tensor_core_status() {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_tc_dev_err, sizeof(int)) != cudaSuccess) return -1;
-  if (v) {
-    const int zero = 0;
-    cudaMemcpyToSymbol(g_tc_dev_err, &zero, sizeof(int));
-  }
-  return v;
-}
-
-// PLE_BACKWARD_KERNEL: "tensor" selects the tensor-core backward, anything else the sorted one.
-int backward_kernel_mode() {
-  const char* v = getenv("PLE_BACKWARD_KERNEL");
-  return (v != nullptr && strcmp(v, "tensor") == 0) ? 2 : 1;
+  return true;
 }
 
 int bwd_finalize(const BwdArgs& a, int grid, cudaStream_t st) {
   const int64_t rows = (int64_t)a.F * (a.B + 3) * a.D;
   const int blocks = (int)min64(ceil_div<int64_t>(rows, 256), 4L * device_sm_count());
-  ple_bwd_finalize_kernel<<<blocks, 256, 0, st>>>(a, grid);
+  ple_bwd_finalize_kernel<<<blocks, 256, 0, st>>>(a, grid / a.group);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? PLE_OK : set_cuda_error(e, "backward finalize launch");
 }

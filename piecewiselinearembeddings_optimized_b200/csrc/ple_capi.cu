@@ -34,16 +34,22 @@ constexpr int kMaxDevices = 64;
 DevProps g_props[kMaxDevices];
 std::once_flag g_once[kMaxDevices];
 
+// Without a visible device (host-side size queries on a machine with no GPU) the
+// properties of the B200 this library is built for: 148 SMs, 227 KiB of opt-in
+// shared memory per block.
+constexpr int kDefaultSms = 148;
+constexpr size_t kDefaultSmemOptin = 232448;
+
 const DevProps& props() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
   std::call_once(g_once[dev], [dev] {
     int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    g_props[dev].sms = v > 0 ? v : 1;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 0;
+    g_props[dev].sms = v > 0 ? v : kDefaultSms;
     v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    g_props[dev].smem_optin = v > 0 ? (size_t)v : 48 * 1024;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+    g_props[dev].smem_optin = v > 0 ? (size_t)v : kDefaultSmemOptin;
   });
   return g_props[dev];
 }
@@ -98,17 +104,15 @@ int device_sm_count() { return props().sms; }
 size_t device_max_smem_optin() { return props().smem_optin; }
 
 // ---------------------------------------------------------------- no-allocation backward
-// The scratch lives in this module's static device memory; its address is
-// looked up once per device and cached.
+// The scratch lives in this module's static device memory; its device address
+// is looked up with the device current and cached per device.  Only a
+// successful lookup is cached: a call that failed (for example one made
+// during a stream capture) leaves the slot empty and the next call retries.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[PLE_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-struct ScratchSlot {
-  std::once_flag once;
-  void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-ScratchSlot g_scratch[kMaxDevices];
+std::mutex g_scratch_mu[kMaxDevices];
+void* g_scratch_ptr[kMaxDevices] = {};
 }  // namespace
 
 static int noalloc_scratch(void** ptr) {
@@ -116,14 +120,15 @@ static int noalloc_scratch(void** ptr) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return set_error(PLE_ERR_UNSUPPORTED, "device ordinal above 63");
-  ScratchSlot& slot = g_scratch[dev];
-  std::call_once(slot.once, [&slot] {
-    slot.err = cudaGetSymbolAddress(&slot.ptr, g_noalloc_scratch);
-  });
-  if (slot.err != cudaSuccess || slot.ptr == nullptr)
-    return set_cuda_error(slot.err != cudaSuccess ? slot.err : cudaErrorInvalidSymbol,
-                          "cudaGetSymbolAddress(no-allocation scratch)");
-  *ptr = slot.ptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mu[dev]);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    if (p == nullptr) return set_error(PLE_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch) returned null");
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
   return PLE_OK;
 }
 
@@ -134,8 +139,6 @@ using namespace ple;
 extern "C" {
 
 int ple_abi_version(void) { return PLE_ABI_VERSION; }
-
-int ple_tensor_core_status(void) { return tensor_core_status(); }
 
 int ple_linear_status(void) { return linear_status(); }
 
@@ -283,6 +286,8 @@ static int backward_impl(const void* g, int grad_dtype, const float* x, const fl
   a.grad_x = grad_x; a.grad_W = grad_W; a.grad_bias = grad_bias; a.grad_w0 = grad_w0; a.grad_b0 = grad_b0;
   a.ws = static_cast<float*>(ws); a.ws_bytes = ws_bytes;
   a.N = N; a.F = (int)F; a.B = (int)B; a.D = (int)D; a.epi = epi; a.relu = relu ? 1 : 0;
+  a.g_wide = aligned(g, 32) ? 1 : 0;  // 32-byte gradient chunks (a whole sector) may be read at once
+  a.gx_vec4 = (grad_x != nullptr && aligned(grad_x, 16) && F % 4 == 0) ? 1 : 0;
   return launch_backward(a, compute_dtype, grad_dtype, vec, s);
 }
 
@@ -389,9 +394,11 @@ int ple_embeddings_backward_noalloc(const void* grad_output, int grad_dtype, con
                                     float* grad_weight, float* grad_bias, float* grad_w0, float* grad_b0,
                                     void* stream) {
   g_msg[0] = 0;
-  int st = check_sizes(batch, n_features, max_n_bins, d_embedding);
+  // the same size limits as ple_embeddings_backward (more than 256 bins only for the bare x_ple op)
+  int st = check_sizes(batch, n_features, max_n_bins, d_embedding,
+                       epilogue == kEpiNone && !activation ? kWideMaxBins : 256);
   if (st) return st;
-  const size_t need = backward_workspace_bytes(batch < 1 ? 1 : batch, n_features, max_n_bins, d_embedding);
+  const size_t need = ple_backward_workspace_size(batch, n_features, max_n_bins, d_embedding);
   if (need > PLE_NOALLOC_SCRATCH_BYTES) {
     snprintf(g_msg, sizeof(g_msg),
              "ple_embeddings_backward_noalloc: this shape needs %zu bytes of workspace, more than the %zu-byte "

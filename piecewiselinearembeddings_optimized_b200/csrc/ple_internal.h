@@ -60,9 +60,14 @@ struct BwdArgs {
   int64_t N;
   int F, B, D;
   int epi, relu;
-  // filled by the launcher (Fc = features per chunk; the sorted kernel uses 1 << lgFc)
-  int lgFc, lgWf, lgSt, n_chunks, max_segs, pow2, x_vec4, Fc;
-  int lgk;  // sorted kernel: 2^lgk - 1 >= B - 1 interior-edge search keys
+  // filled by the launcher: Fc = 1 << lgFc features per chunk, 1 << lgWf warps per feature, tiles of
+  // 1 << lgSt samples, 2^lgk - 1 >= B - 1 interior-edge search keys; `group` CTAs (one chunk each) share
+  // the sample ranges of a group of chunks; g_wide: 32-byte gradient chunks may be read at once
+  int lgFc, lgWf, lgSt, n_chunks, max_segs, Fc;
+  int lgk;
+  int group, n_groups, g_wide;
+  int g_prefetch;  // the gradient tensor map is valid (per-tile L2 prefetch)
+  int gx_vec4;     // grad_x rows may be stored 16 bytes at a time (16-byte aligned, F % 4 == 0)
 };
 
 struct EncArgs {
@@ -115,7 +120,6 @@ size_t wide_workspace_bytes(int64_t F, int64_t B, int64_t D);
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
-int tensor_core_status();
 int launch_linear(const LinearCall& c, cudaStream_t st);
 size_t linear_workspace_bytes(int64_t F, int64_t B, int64_t D, int64_t H, int compute_dtype);
 int linear_status();

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from piecewiselinearembeddings_optimized_b200 import _native
+from tests import _placeholder
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADERS = sorted((ROOT / "include").glob("*.h"))
@@ -40,7 +41,14 @@ def test_abi_version_and_status_strings():
     assert lib.ple_status_string(99) == b"unknown status"
 
 
-FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails before any device access
+FAKE = None  # placeholder pointer for calls refused before any launch (set per test)
+
+
+@pytest.fixture(autouse=True)
+def _placeholder_pointer():
+    """A real device buffer when a GPU is present (tests/_placeholder.py), else a non-null dummy."""
+    global FAKE
+    FAKE = _placeholder.ptr()
 
 
 @pytest.mark.parametrize("n,f,b,d,code,msg", [
@@ -100,6 +108,30 @@ def test_backward_requires_workspace_before_any_launch():
     st = lib.ple_backward(FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, None, 3, 4, 3, 4, 8, FAKE, FAKE,
                           None, 0, None)
     assert st == 5
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def test_noalloc_refuses_shapes_beyond_the_scratch():
+    """ple_embeddings_backward_noalloc refuses a shape whose workspace exceeds its
+    built-in scratch, before any launch, naming the size and the entry point to use."""
+    lib = _native.capi()
+    # many small features: more than 16 MiB of partial sums whatever the device properties
+    for n, f, b, d in ((64, 1 << 20, 16, 8), (64, 1024, 256, 32), (256, 8192, 128, 32)):
+        need = lib.ple_backward_workspace_size(n, f, b, d)
+        if need > NOALLOC_SCRATCH_BYTES:
+            break
+    assert need > NOALLOC_SCRATCH_BYTES
+    st = lib.ple_embeddings_backward_noalloc(FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, None, 0, 0, 0,
+                                             n, f, b, d, None, 3, FAKE, FAKE, None, None, None, None)
+    assert st == 5
+    msg = lib.ple_last_error_message().decode()
+    assert str(need) in msg and "ple_embeddings_backward" in msg
+    # more than 256 bins: accepted for the bare op (the wide-bin kernels) but refused with an epilogue
+    st = lib.ple_embeddings_backward_noalloc(FAKE, 0, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, 1, 1, 0,
+                                             4, 3, 300, 8, None, 3, FAKE, FAKE, FAKE, None, None, None)
+    assert st == 4 and b"max_n_bins > 256" in lib.ple_last_error_message()
 
 
 # ---------------------------------------------------------------- GPU: direct calls

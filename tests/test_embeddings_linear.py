@@ -14,7 +14,6 @@ autocast.  CPU: workspace sizing and argument validation of the C ABI.
 """
 from __future__ import annotations
 
-import ctypes
 
 import numpy as np
 import pytest
@@ -23,11 +22,18 @@ torch = pytest.importorskip("torch")
 
 from oracle import ple_oracle as o  # noqa: E402
 from piecewiselinearembeddings_optimized_b200 import _native, workloads  # noqa: E402
-from tests import cases  # noqa: E402
+from tests import _placeholder, cases  # noqa: E402
 
 EPI = {"A": 1, "B": 2}
 TORCH_DT = {"f32": torch.float32, "bf16": torch.bfloat16}
-FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails before any device access
+FAKE = None  # placeholder pointer for calls refused before any launch (set per test)
+
+
+@pytest.fixture(autouse=True)
+def _placeholder_pointer():
+    """A real device buffer when a GPU is present (tests/_placeholder.py), else a non-null dummy."""
+    global FAKE
+    FAKE = _placeholder.ptr()
 
 
 # ---------------------------------------------------------------- CPU: C ABI sizing and validation
@@ -41,8 +47,9 @@ def test_workspace_size_and_unsupported_shapes():
     assert lib.ple_embeddings_linear_workspace_size(8, 300, 16, 64, _native.DTYPE_BF16) == 0
 
 
-def _call(lib, *, epi=1, bias=FAKE, compute=_native.DTYPE_BF16, wdt=_native.DTYPE_BF16, out=_native.DTYPE_F32,
-          n=4, h=32):
+def _call(lib, *, epi=1, bias="placeholder", compute=_native.DTYPE_BF16, wdt=_native.DTYPE_BF16,
+          out=_native.DTYPE_F32, n=4, h=32):
+    bias = FAKE if bias == "placeholder" else bias
     return lib.ple_embeddings_linear_forward(FAKE, FAKE, FAKE, FAKE, FAKE, bias, None, None, epi, 1, compute,
                                              n, 3, 4, 8, FAKE, wdt, None, h, out, FAKE, FAKE, 1 << 20, None)
 

@@ -5,7 +5,6 @@ layouts, on the reference's bin cases plus edge ties, +-inf and NaN; the
 gradient with respect to x matches the clamp rule (GPU)."""
 from __future__ import annotations
 
-import ctypes
 
 import numpy as np
 import pytest
@@ -92,7 +91,9 @@ def test_encoding_capi_rejects_bad_layouts():
     from piecewiselinearembeddings_optimized_b200 import _native
 
     lib = _native.capi()
-    fake = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+    from tests import _placeholder
+
+    fake = _placeholder.ptr()  # real device memory when a GPU is present; refused before any launch
     assert lib.ple_encoding_forward(fake, fake, fake, fake, fake, 7, 4, 3, 4, 12, 0, fake, None) == 1
     assert lib.ple_encoding_forward(fake, fake, fake, fake, fake, 1, 4, 3, 4, 11, 0, fake, None) == 2
     assert lib.ple_encoding_forward(fake, fake, fake, fake, None, 0, 4, 3, 4, 10, 0, fake, None) == 1

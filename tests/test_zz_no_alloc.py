@@ -1,12 +1,19 @@
 """ple_embeddings_backward_noalloc: the fused backward with the library's
-built-in scratch instead of a caller workspace.  Its results must equal those
-of ple_embeddings_backward (same kernels, deterministic) on two calls in a
-row, and shapes whose workspace exceeds the scratch must be refused before
-any launch.  The file name sorts last so that the test also runs after every
-other GPU test in the same process."""
-from __future__ import annotations
+built-in scratch instead of a caller workspace, for callers that cannot hand
+over device memory of their own (plain C FFI hosts without a device
+allocator, serving processes that reserve all memory at start-up).
 
-import ctypes
+Its results must equal those of ple_embeddings_backward on two calls in a
+row, and again after calls of the same and of another shape have left
+garbage (NaN partial sums) in the shared scratch: every scratch slot the backward reads must be
+written earlier in the same call.  The main kernels are deterministic, so
+their results are compared bitwise; the wide-bin path (more than 256 bins)
+sums with atomics and is compared within the gradient tolerance of the parity
+tests (rtol 1e-4, atol 1e-5).  The refusal of shapes beyond the scratch needs
+no device and is a CPU test in test_capi.py.  The file name sorts last so that
+these tests also run after every other GPU test in the same process.
+"""
+from __future__ import annotations
 
 import numpy as np
 import pytest
@@ -16,7 +23,7 @@ from piecewiselinearembeddings_optimized_b200 import _native
 pytestmark = pytest.mark.gpu
 
 SCRATCH_BYTES = 16 << 20
-PLE_ERR_WORKSPACE = 5
+GRAD_NAMES = ("grad_x", "grad_W", "grad_bias", "grad_w0", "grad_b0")
 
 
 def _inputs(torch, dev, name, n, f):
@@ -31,60 +38,108 @@ def _inputs(torch, dev, name, n, f):
     return wl, g, [T(a) for a in (wl.x, edges, inv_w, nb, wl.weight, wl.bias, wl.w0, wl.b0)]
 
 
-def _grads(torch, dev, wl):
-    f, b, d = wl.f, wl.max_n_bins, wl.d
-    return [torch.full(s, float("nan"), device=dev) for s in ((wl.n, f), (f, b, d), (f, d), (f, d), (f, d))]
+class _Call:
+    """Argument lists of one backward configuration for both entry points."""
+
+    def __init__(self, torch, dev, wl, g, tensors, epi, relu):
+        self.torch, self.dev, self.wl, self.g = torch, dev, wl, g
+        self.x, self.e, self.r, self.nb, self.w, self.bias, self.w0, self.b0 = tensors
+        self.epi, self.relu = epi, relu
+        self.code = {torch.float32: 0, torch.bfloat16: 2}[g.dtype]
+        self.qcode = 2 if wl.mode == "bf16" else 0
+        self.shape = (wl.n, wl.f, wl.max_n_bins, wl.d)
+
+    def head(self, g=None):
+        P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        g = self.g if g is None else g
+        return (P(g), self.code, P(self.x), P(self.e), P(self.r), P(self.nb), P(self.w), P(self.bias), P(self.w0),
+                P(self.b0), self.epi, self.relu, self.qcode, *self.shape, None, 3)
+
+    def grads(self):
+        n, f, b, d = self.shape
+        return [self.torch.full(s, float("nan"), device=self.dev) for s in ((n, f), (f, b, d), (f, d), (f, d), (f, d))]
+
+    def wanted(self, name):
+        return ((name != "grad_bias" or self.epi == 1) and (name not in ("grad_w0", "grad_b0") or self.epi == 2))
 
 
-@pytest.mark.parametrize("name,n,f", [("c1", 1000, None), ("c2", 4096, 32), ("c4", 8192, 64)])
-def test_noalloc_matches_workspace_entry_point_twice(cuda_device, name, n, f):
+def _run_reference(lib, c, stream):
+    ws_bytes = lib.ple_backward_workspace_size(*c.shape)
+    ws = c.torch.empty(ws_bytes, dtype=c.torch.uint8, device=c.dev)
+    out = c.grads()
+    _native.check(lib.ple_embeddings_backward(*c.head(), *[t.data_ptr() for t in out], ws.data_ptr(), ws_bytes,
+                                              stream), "ple_embeddings_backward")
+    return out
+
+
+def _run_noalloc(lib, c, stream, g=None):
+    out = c.grads()
+    _native.check(lib.ple_embeddings_backward_noalloc(*c.head(g), *[t.data_ptr() for t in out], stream),
+                  "ple_embeddings_backward_noalloc")
+    return out
+
+
+def _compare(torch, c, ref, got, exact, what):
+    for name, a, b in zip(GRAD_NAMES, ref, got):
+        if not c.wanted(name):
+            continue
+        if exact:
+            assert torch.equal(a, b), f"{what}: {name} differs from ple_embeddings_backward"
+        else:
+            torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-5, msg=f"{what}: {name}")
+
+
+CASES = [  # name, n, f, epilogue, relu, exact
+    ("c1", 1000, None, None, None, True),
+    ("c2", 4096, 32, None, None, True),
+    ("c4", 8192, 64, None, None, True),
+    ("wide", 512, 3, 0, 0, False),  # 300 bins, bare x_ple op: the wide-bin kernels
+]
+
+
+@pytest.mark.parametrize("name,n,f,epi,relu,exact", CASES, ids=[c[0] for c in CASES])
+def test_noalloc_matches_workspace_entry_point(cuda_device, name, n, f, epi, relu, exact):
     import torch
 
     lib = _native.capi()
-    wl, g, (x, e, r, nb, w, bias, w0, b0) = _inputs(torch, cuda_device, name, n, f)
-    P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-    code = {torch.float32: 0, torch.bfloat16: 2}
-    gcode = code[g.dtype]
-    qcode = 2 if wl.mode == "bf16" else 0
-    epi = 2 if wl.version == "B" else 1
-    F, B, D = wl.f, wl.max_n_bins, wl.d
-    assert lib.ple_backward_workspace_size(wl.n, F, B, D) <= SCRATCH_BYTES
     stream = torch.cuda.current_stream().cuda_stream
+    if name == "wide":
+        from oracle import ple_oracle as o
+        from tests import cases
 
-    def head():
-        return (P(g), gcode, P(x), P(e), P(r), P(nb), P(w), P(bias), P(w0), P(b0), epi, int(wl.activation), qcode,
-                wl.n, F, B, D, None, 3)
+        rng = np.random.default_rng(5)
+        # ragged wide features (300, 5 and 120 bins): cumulative sums of seeded steps, as the parity tests
+        bins = [(np.cumsum(rng.random(k + 1) + 0.01) - 0.3 * k).astype(np.float32) for k in (300, 5, 120)][:f]
+        wl_x = cases.sample_x(bins, n, 12)
+        edges, inv_w, nb = o.pad_bins(bins)
+        B = edges.shape[1] - 1
+        W = rng.uniform(0.05, 0.25, (f, B, 8)).astype(np.float32)
+        T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)  # noqa: E731
 
-    ws_bytes = lib.ple_backward_workspace_size(wl.n, F, B, D)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda_device)
-    ref = _grads(torch, cuda_device, wl)
-    _native.check(lib.ple_embeddings_backward(*head(), *[P(t) for t in ref], P(ws), ws_bytes, stream),
-                  "ple_embeddings_backward")
+        class _WL:
+            pass
+
+        wl = _WL()
+        wl.n, wl.f, wl.max_n_bins, wl.d, wl.mode = n, f, B, 8, "f32"
+        g = T(rng.standard_normal((n, f, 8)).astype(np.float32))
+        c = _Call(torch, cuda_device, wl, g, [T(a) for a in (wl_x, edges, inv_w, nb, W)] + [None, None, None],
+                  epi, relu)
+    else:
+        wl, g, tensors = _inputs(torch, cuda_device, name, n, f)
+        c = _Call(torch, cuda_device, wl, g, tensors, 2 if wl.version == "B" else 1, int(wl.activation))
+    assert lib.ple_backward_workspace_size(*c.shape) <= SCRATCH_BYTES
+    ref = _run_reference(lib, c, stream)
+    # two calls in a row
     for call in range(2):
-        got = _grads(torch, cuda_device, wl)
-        _native.check(lib.ple_embeddings_backward_noalloc(*head(), *[P(t) for t in got], stream),
-                      "ple_embeddings_backward_noalloc")
+        got = _run_noalloc(lib, c, stream)
         torch.cuda.synchronize()
-        for name_, a, b in zip(("grad_x", "grad_W", "grad_bias", "grad_w0", "grad_b0"), ref, got):
-            wanted = (name_ != "grad_bias" or epi == 1) and (name_ not in ("grad_w0", "grad_b0") or epi == 2)
-            if wanted:
-                assert torch.equal(a, b), f"call {call}: {name_} differs from ple_embeddings_backward"
-
-
-def test_noalloc_refuses_shapes_beyond_the_scratch(cuda_device):
-    import torch
-
-    lib = _native.capi()
-    # many small feature chunks per CTA range give many partial slots; the first plannable shape above the scratch
-    for n, f, b, d in ((64, 1024, 256, 32), (256, 8192, 128, 32), (1 << 20, 8192, 64, 64)):
-        need = lib.ple_backward_workspace_size(n, f, b, d)
-        if need > SCRATCH_BYTES:
-            break
-    assert need > SCRATCH_BYTES
-    fake = ctypes.c_void_p(0x1000)  # never dereferenced: the size check runs before any device access
-    st = lib.ple_embeddings_backward_noalloc(fake, 0, fake, fake, fake, fake, fake, None, None, None, 0, 0, 0,
-                                             n, f, b, d, None, 3, fake, fake, None, None, None, None)
-    assert st == PLE_ERR_WORKSPACE
-    msg = lib.ple_last_error_message().decode()
-    assert str(need) in msg and "ple_embeddings_backward" in msg
+        _compare(torch, c, ref, got, exact, f"call {call}")
+    # garbage in the shared scratch: NaN partial sums from a call of the same shape (exactly the slots the
+    # checked call uses) and from a call of another shape, both with a NaN upstream gradient
+    _run_noalloc(lib, c, stream, g=torch.full_like(c.g, float("nan")))
+    other_wl, other_g, other_t = _inputs(torch, cuda_device, "c1", 777, 5)
+    other = _Call(torch, cuda_device, other_wl, other_g.fill_(float("nan")), other_t, 2, 1)
+    _run_noalloc(lib, other, stream)
+    got = _run_noalloc(lib, c, stream)
     torch.cuda.synchronize()
+    _compare(torch, c, ref, got, exact, "after NaN calls of the same and of another shape")
