@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c4", action="store_true", help="skip the c4 north-star figures of the default run")
+    ap.add_argument("--no-reference-cuda", action="store_true",
+                    help="reference arm: skip the GPU timing of the reference's own CUDA ops")
     ap.add_argument("--consumer", type=int, default=None, metavar="H",
                     help="time the module fused into a following Linear(F*D -> H) (forward, bf16 autocast "
                          "semantics) against the unfused embeddings kernel + cuBLAS, one GPU")
@@ -163,10 +165,35 @@ def reference_arm(args, ws, rank):
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference CPU path = upstream rtdl_num_embeddings (not installable offline); timed here as "
                 "its dense algorithm restated in torch CPU ops (oracle/cpu_baseline.py)",
-        "wall_s": round(time.time() - t0, 1),
     }
+    if not args.no_reference_cuda:
+        line["reference_cuda"] = reference_cuda_timings(args)
+    line["wall_s"] = round(time.time() - t0, 1)
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_cuda_timings(args) -> dict:
+    """The reference's own CUDA ops (compiled from its sources into oracle/_ref) timed on GPU 0 for the
+    c4 shape and the per-GPU shard of c5 at 8 GPUs (131,072 rows; the reference's unfused epilogue
+    holds several [N, F, D] temporaries, too many for the full 1,048,576-row batch), each in its own
+    process (the reference registers the same op namespace as this project).  A secondary, GPU-side
+    baseline reported beside the CPU figure; `value` stays the CPU figure."""
+    out = {}
+    script = ROOT / "oracle" / "time_reference_cuda.py"
+    for key, cfg, batch in (("c4", "c4", None), ("c5_shard_of_8", "c5", 131072)):
+        cmd = [sys.executable, str(script), "--config", cfg, "--steps", str(max(5, args.steps)),
+               "--warmup", str(max(3, args.warmup))]
+        if batch:
+            cmd += ["--batch", str(batch)]
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+            lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+            out[key] = json.loads(lines[-1]) if (r.returncode == 0 and lines) else {
+                "unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip()[-300:]}"}
+        except (OSError, subprocess.TimeoutExpired, ValueError) as e:
+            out[key] = {"unavailable": f"{type(e).__name__}: {e}"}
+    return out
 
 
 def consumer_bench(args) -> int:

@@ -11,9 +11,11 @@ own build system (``setup.py``) is not used.  Outputs go only to
 
 The library registers the op namespace ``rtdl_num_embeddings_cuda`` - the
 same namespace as the product - so it must be loaded in a separate process
-(``tests/golden/make_golden.py`` and ``tests/_ref_runner.py`` do that).
+(``tests/golden/make_golden.py`` and ``oracle/time_reference_cuda.py`` do that).
 
-Usage: ``python oracle/build_ref.py [--reference DIR]``; a no-op when the
+Usage: ``python oracle/build_ref.py [--reference DIR]``.  The reference
+project is found at ``--reference``, else at ``$PLE_REFERENCE_DIR``, else in a
+directory named ``reference`` beside this repository.  A no-op when the
 reference sources are absent (e.g. on a GPU box, which uses the prebuilt
 file).
 """
@@ -29,7 +31,12 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 LIB = OUT_DIR / "rtdl_ref_ops.so"
-DEFAULT_REFERENCE = Path("/root/reference")
+
+
+def default_reference() -> Path:
+    """$PLE_REFERENCE_DIR, else a directory named ``reference`` beside this repository."""
+    env = os.environ.get("PLE_REFERENCE_DIR")
+    return Path(env) if env else HERE.parent.parent / "reference"
 
 
 def _torch_paths():
@@ -42,8 +49,8 @@ def _torch_paths():
     return inc, libdir, abi
 
 
-def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path | None:
-    csrc = reference / "csrc"
+def build(reference: Path | None = None, force: bool = False) -> Path | None:
+    csrc = (reference or default_reference()) / "csrc"
     sources = [csrc / "ops.cpp", csrc / "forward_cuda.cu", csrc / "backward_cuda.cu"]
     if not all(s.exists() for s in sources):
         return LIB if LIB.exists() else None
@@ -89,7 +96,7 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path | No
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", type=Path, default=None)
     ap.add_argument("--force", action="store_true")
     args = ap.parse_args(argv)
     lib = build(args.reference, args.force)

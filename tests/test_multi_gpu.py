@@ -1,7 +1,8 @@
-"""Data-parallel step on 2+ GPUs: each rank runs the fused forward/backward on
-its batch shard and one NCCL all-reduce of the packed parameter gradients;
-the result must equal the single-GPU full-batch gradients.  Skipped with
-fewer than two visible GPUs."""
+"""Data-parallel step on 2+ GPUs: each rank runs the fused backward on its
+batch shard and one NCCL all-reduce of the packed parameter gradients.  The
+reduced gradients must match the CPU oracle's full-batch gradients (and the
+single-GPU full-batch kernel), and each rank's grad_x rows the oracle's rows
+of its shard.  Skipped with fewer than two visible GPUs."""
 from __future__ import annotations
 
 import datetime
@@ -48,8 +49,9 @@ def _rank_main(rank, ws, port, q):
         tx, tg = T(wl.x[lo:hi]), T(g[lo:hi])
         params = [torch.nn.Parameter(torch.empty_like(t)) for t in (tw, tw0, tb0)]
         bucket = GradientBucket(params)
-        _, gw, _, gw0, gb0 = ops.embeddings_backward(tg, tx, te, tr, tn, tw, None, tw0, tb0, None, 2, True,
-                                                      torch.float32, False, True, False, True)
+        gxs, gw, _, gw0, gb0 = ops.embeddings_backward(tg, tx, te, tr, tn, tw, None, tw0, tb0, None, 2, True,
+                                                        torch.float32, True, True, False, True)
+        shard_gx = gxs.cpu().numpy()
         for v, src in zip(bucket.views, (gw, gw0, gb0)):
             v.copy_(src)
         bucket.all_reduce()
@@ -65,9 +67,9 @@ def _rank_main(rank, ws, port, q):
             tmax = max(1.0, float(np.abs(o.position(wl.x, k, edges, inv_w)).max()))
             bounds = [np.broadcast_to(absg[:, None, :] * tmax, fw.shape), np.einsum("nfd,nf->fd", np.abs(g),
                       np.abs(wl.x)), absg]
-            q.put((rank, "ok", reduced, full, bounds))
+            q.put((rank, "ok", (reduced, shard_gx, lo, hi), full, bounds))
         else:
-            q.put((rank, "ok", reduced, None, None))
+            q.put((rank, "ok", (reduced, shard_gx, lo, hi), None, None))
         torch.cuda.synchronize()
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e), None, None))
@@ -91,6 +93,18 @@ def test_two_rank_allreduce_matches_full_batch():
         p.join(timeout=120)
     assert all(r[1] == "ok" for r in res), [r[2] for r in res if r[1] != "ok"]
     full, bounds = res[0][3], res[0][4]
-    for rank, _, reduced, _, _ in res:
-        for got, ref, bd, name in zip(reduced, full, bounds, ("grad_W", "grad_w0", "grad_b0")):
-            o.assert_reduction_close(got, ref, 2 * bd, err_msg=f"rank {rank} {name}")
+    # the CPU oracle's full-batch gradients (dense upstream formulation, float64 accumulation)
+    from piecewiselinearembeddings_optimized_b200 import workloads
+
+    wl = workloads.make_workload("c5", n=8192, f=64)
+    g = workloads.make_grad(wl)
+    edges, inv_w, nb = o.pad_bins(wl.bins)
+    ref = o.embeddings_backward(g, wl.x, edges, inv_w, nb, wl.weight, version="B", activation=True, w0=wl.w0,
+                                b0=wl.b0)
+    oracle = (ref["grad_W"], ref["grad_w0"], ref["grad_b0"])
+    for rank, _, (reduced, shard_gx, lo, hi), _, _ in res:
+        for got, one_gpu, want, bd, name in zip(reduced, full, oracle, bounds, ("grad_W", "grad_w0", "grad_b0")):
+            o.assert_reduction_close(got, want, 2 * bd, err_msg=f"rank {rank} {name} vs the oracle")
+            o.assert_reduction_close(got, one_gpu, 2 * bd, err_msg=f"rank {rank} {name} vs one GPU")
+        np.testing.assert_allclose(shard_gx, ref["grad_x"][lo:hi], rtol=1e-4, atol=1e-5,
+                                   err_msg=f"rank {rank} grad_x rows {lo}..{hi}")

@@ -8,8 +8,9 @@ row, and again after calls of the same and of another shape have left
 garbage (NaN partial sums) in the shared scratch: every scratch slot the backward reads must be
 written earlier in the same call.  The main kernels are deterministic, so
 their results are compared bitwise; the wide-bin path (more than 256 bins)
-sums with atomics and is compared within the gradient tolerance of the parity
-tests (rtol 1e-4, atol 1e-5).  The refusal of shapes beyond the scratch needs
+sums grad_W with atomics (any order) and is compared within the parity tests'
+summation-order bound (rtol 1e-4, atol 1e-5 plus 2^-20 of the sum of the
+terms' magnitudes), its other gradients within rtol 1e-4, atol 1e-5.  The refusal of shapes beyond the scratch needs
 no device and is a CPU test in test_capi.py.  The file name sorts last so that
 these tests also run after every other GPU test in the same process.
 """
@@ -79,12 +80,16 @@ def _run_noalloc(lib, c, stream, g=None):
     return out
 
 
-def _compare(torch, c, ref, got, exact, what):
+def _compare(torch, c, ref, got, exact, what, bounds=None):
+    from oracle import ple_oracle as o
+
     for name, a, b in zip(GRAD_NAMES, ref, got):
         if not c.wanted(name):
             continue
         if exact:
             assert torch.equal(a, b), f"{what}: {name} differs from ple_embeddings_backward"
+        elif name in bounds:  # sums in atomic order: within the summation-order bound of the parity tests
+            o.assert_reduction_close(b.cpu().numpy(), a.cpu().numpy(), bounds[name], err_msg=f"{what}: {name}")
         else:
             torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-5, msg=f"{what}: {name}")
 
@@ -124,16 +129,22 @@ def test_noalloc_matches_workspace_entry_point(cuda_device, name, n, f, epi, rel
         g = T(rng.standard_normal((n, f, 8)).astype(np.float32))
         c = _Call(torch, cuda_device, wl, g, [T(a) for a in (wl_x, edges, inv_w, nb, W)] + [None, None, None],
                   epi, relu)
+        # 2 x sum of |terms| of each grad_W element: |g| times the largest |t| of the feature's samples
+        gn = g.cpu().numpy()
+        k = o.bin_index(wl_x, edges, nb)
+        tmax = np.maximum(1.0, np.abs(o.position(wl_x, k, edges, inv_w)).max(axis=0))
+        bounds = {"grad_W": np.broadcast_to((np.abs(gn).sum(0) * tmax[:, None])[:, None, :], (f, B, 8)) * 2}
     else:
         wl, g, tensors = _inputs(torch, cuda_device, name, n, f)
         c = _Call(torch, cuda_device, wl, g, tensors, 2 if wl.version == "B" else 1, int(wl.activation))
+        bounds = {}
     assert lib.ple_backward_workspace_size(*c.shape) <= SCRATCH_BYTES
     ref = _run_reference(lib, c, stream)
     # two calls in a row
     for call in range(2):
         got = _run_noalloc(lib, c, stream)
         torch.cuda.synchronize()
-        _compare(torch, c, ref, got, exact, f"call {call}")
+        _compare(torch, c, ref, got, exact, f"call {call}", bounds)
     # garbage in the shared scratch: NaN partial sums from a call of the same shape (exactly the slots the
     # checked call uses) and from a call of another shape, both with a NaN upstream gradient
     _run_noalloc(lib, c, stream, g=torch.full_like(c.g, float("nan")))
@@ -142,4 +153,4 @@ def test_noalloc_matches_workspace_entry_point(cuda_device, name, n, f, epi, rel
     _run_noalloc(lib, other, stream)
     got = _run_noalloc(lib, c, stream)
     torch.cuda.synchronize()
-    _compare(torch, c, ref, got, exact, "after NaN calls of the same and of another shape")
+    _compare(torch, c, ref, got, exact, "after NaN calls of the same and of another shape", bounds)
