@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define PLE_ABI_VERSION 6
+#define PLE_ABI_VERSION 7
 
 /* Element types (codes shared by every entry point). */
 enum {
@@ -116,6 +116,21 @@ int ple_forward(const float* x, const float* bin_edges, const float* inv_bin_wid
  */
 size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t max_n_bins,
                                    int64_t d_embedding);
+
+/*
+ * Which kernel ple_backward / ple_embeddings_backward run for these sizes on
+ * the current device: PLE_BACKWARD_HISTOGRAM (natural sample order, per-warp
+ * bin sums in shared memory; d_embedding 8, 16 or 24, at most 256 bins),
+ * PLE_BACKWARD_SORTED (per-tile counting sort and segmented walk; the other
+ * shapes up to 256 bins, or every shape when the environment variable
+ * PLE_BACKWARD_KERNEL=sorted is set when the library first plans a backward),
+ * PLE_BACKWARD_WIDE (more than 256 bins), or minus the PLE_ERR_* status of
+ * sizes the backward refuses.  Both fused kernels give bitwise-deterministic results.
+ */
+#define PLE_BACKWARD_SORTED 0
+#define PLE_BACKWARD_HISTOGRAM 1
+#define PLE_BACKWARD_WIDE 2
+int ple_backward_kernel_kind(int64_t n_features, int64_t max_n_bins, int64_t d_embedding);
 
 /*
  * x_ple backward (reference op rtdl_num_embeddings_cuda::backward).

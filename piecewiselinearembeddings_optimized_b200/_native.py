@@ -63,6 +63,8 @@ def capi() -> ctypes.CDLL:
     lib.ple_forward.argtypes = [P, P, P, P, P, I64, I64, I64, I64, I, P, I, P, P]
     lib.ple_backward_workspace_size.restype = SZ
     lib.ple_backward_workspace_size.argtypes = [I64, I64, I64, I64]
+    lib.ple_backward_kernel_kind.restype = I
+    lib.ple_backward_kernel_kind.argtypes = [I64, I64, I64]
     lib.ple_backward.restype = I
     lib.ple_backward.argtypes = [P, I, P, P, P, P, P, P, I, I64, I64, I64, I64, P, P, P, SZ, P]
     lib.ple_embeddings_forward.restype = I

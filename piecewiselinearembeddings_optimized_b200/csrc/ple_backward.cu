@@ -15,6 +15,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "ple_backward_hist.cuh"
 #include "ple_backward_impl.cuh"
 
 namespace ple {
@@ -133,14 +134,76 @@ static size_t ws_bytes_for(const BwdArgs& a, int grid) {
   return (size_t)grid * a.max_segs * ((size_t)a.Fc * (a.B + 3) * a.D) * sizeof(float);
 }
 
+// Histogram kernel: D = 4 VEC with VEC in {2, 4, 6}, at most 256 bins; features per CTA (4, 2, 1, preferred
+// in that order: whole 16-byte x / grad_x pieces per sample) and the longest tile (an even number of
+// 32-sample batches per warp) whose layout fits.
+static bool hist_plan(BwdArgs& a, size_t* smem_out) {
+  const int vec = a.D / kHistNC;
+  if (a.D % kHistNC != 0 || (vec != 2 && vec != 4 && vec != 6) || a.B > 256 || a.B < 1) return false;
+  a.lgk = 0;
+  while ((1 << a.lgk) < a.B) ++a.lgk;
+  const size_t optin = device_max_smem_optin();
+  for (int lgFc = 2; lgFc >= 0; --lgFc) {
+    if (lgFc > 0 && (1 << (lgFc - 1)) >= a.F) continue;
+    const int Fc = 1 << lgFc, Wf = kBwdWarps / Fc;
+    for (int lgSt = 9; (1 << lgSt) >= 64 * Wf; --lgSt) {  // an even number of 32-sample batches per warp
+      const size_t bytes = hist_layout_bytes(a.B, a.D, Fc, 1 << lgSt, 1 << a.lgk, nullptr, nullptr);
+      if (bytes > optin) continue;
+      a.lgFc = lgFc;
+      a.Fc = Fc;
+      a.lgWf = 0;
+      while ((1 << a.lgWf) < Wf) ++a.lgWf;
+      a.lgSt = lgSt;
+      a.n_chunks = (int)ceil_div<int64_t>(a.F, Fc);
+      *smem_out = bytes;
+      return true;
+    }
+  }
+  return false;
+}
+
+// The kernel a backward of this shape runs: the histogram kernel where its plan fits, unless
+// PLE_BACKWARD_KERNEL=sorted (read once) asks for the sorted kernel everywhere.
+static bool use_hist() {
+  static const bool hist = [] {
+    const char* v = getenv("PLE_BACKWARD_KERNEL");
+    return !(v != nullptr && strcmp(v, "sorted") == 0);
+  }();
+  return hist;
+}
+
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D) {
+  size_t best = 0;
   BwdArgs b{};
   b.N = N; b.F = (int)F; b.B = (int)B; b.D = (int)D;
   size_t smem = 0;
-  if (!bwd_plan(b, backward_vec(D, 4), &smem)) return 0;
   int grid = 0;
-  bwd_grid(b, &grid);
-  return ws_bytes_for(b, grid);
+  if (bwd_plan(b, backward_vec(D, 4), &smem)) {
+    bwd_grid(b, &grid);
+    best = ws_bytes_for(b, grid);
+  }
+  BwdArgs h{};
+  h.N = N; h.F = (int)F; h.B = (int)B; h.D = (int)D;
+  if (hist_plan(h, &smem)) {
+    bwd_grid(h, &grid);
+    best = std::max(best, ws_bytes_for(h, grid));
+  }
+  return best;
+}
+
+bool backward_uses_hist(int64_t F, int64_t B, int64_t D) {
+  BwdArgs h{};
+  h.N = 1; h.F = (int)F; h.B = (int)B; h.D = (int)D;
+  size_t smem = 0;
+  return use_hist() && hist_plan(h, &smem);
+}
+
+int hist_prepare(BwdArgs& a, size_t* smem, int* grid) {
+  if (!hist_plan(a, smem)) return set_error(PLE_ERR_UNSUPPORTED, "backward: shape outside the histogram kernel");
+  bwd_grid(a, grid);
+  if (ws_bytes_for(a, *grid) > a.ws_bytes)
+    return set_error(PLE_ERR_WORKSPACE, "backward: workspace smaller than ple_backward_workspace_size()");
+  return PLE_OK;
 }
 
 int bwd_prepare(BwdArgs& a, int vec, size_t* smem, int* grid) {

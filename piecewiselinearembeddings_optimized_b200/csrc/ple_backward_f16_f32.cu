@@ -1,9 +1,9 @@
-// ple_backward_f16_f32.cu - backward kernel instantiations for compute type
+// ple_backward_f16_f32.cu - backward kernel instantiations (histogram and sorted) for compute type
 // __half with gradients in float.
-#include "ple_backward_impl.cuh"
+#include "ple_backward_hist.cuh"
 
 namespace ple {
 
-int launch_bwd_f16_f32(const BwdArgs& a, int vec, cudaStream_t st) { return launch_bwd_dtype<__half, float>(a, vec, st); }
+int launch_bwd_f16_f32(const BwdArgs& a, int vec, cudaStream_t st) { return launch_backward_dtype<__half, float>(a, vec, st); }
 
 }  // namespace ple

@@ -178,8 +178,9 @@ __device__ __forceinline__ float row_sum(float v, int c, int nc) {
 }
 
 // ------------------------------------------------------------------ rows
-// VEC fp32 values of one D-row chunk held as packed pairs (VEC >= 2) or a
-// scalar (VEC == 1), so the arithmetic maps onto fp32x2 instructions.
+// VEC fp32 values of one D-row chunk held as packed pairs (VEC >= 2, even) or
+// a scalar (VEC == 1), so the arithmetic maps onto fp32x2 instructions;
+// shared / global accesses are 16 bytes wide when VEC % 4 == 0, else 8.
 template <int VEC> struct Row {
   static constexpr int NP = VEC >= 2 ? VEC / 2 : 1;
   f2_t p[NP];  // VEC == 1 uses the low half of p[0]
@@ -195,8 +196,9 @@ template <int VEC> struct Row {
         p[e] = v.x;
         p[e + 1] = v.y;
       }
-    } else if constexpr (VEC == 2) {
-      p[0] = *reinterpret_cast<const unsigned long long*>(src);
+    } else if constexpr (VEC % 2 == 0) {
+#pragma unroll
+      for (int e = 0; e < NP; ++e) p[e] = *reinterpret_cast<const unsigned long long*>(src + 2 * e);
     } else {
       p[0] = (f2_t)__float_as_uint(*src);
     }
@@ -209,8 +211,9 @@ template <int VEC> struct Row {
         p[e] = v.x;
         p[e + 1] = v.y;
       }
-    } else if constexpr (VEC == 2) {
-      p[0] = __ldg(reinterpret_cast<const unsigned long long*>(src));
+    } else if constexpr (VEC % 2 == 0) {
+#pragma unroll
+      for (int e = 0; e < NP; ++e) p[e] = __ldg(reinterpret_cast<const unsigned long long*>(src + 2 * e));
     } else {
       p[0] = (f2_t)__float_as_uint(__ldg(src));
     }
@@ -220,8 +223,9 @@ template <int VEC> struct Row {
 #pragma unroll
       for (int e = 0; e < NP; e += 2)
         *reinterpret_cast<ulonglong2*>(dst + 2 * e) = make_ulonglong2(p[e], p[e + 1]);
-    } else if constexpr (VEC == 2) {
-      *reinterpret_cast<unsigned long long*>(dst) = p[0];
+    } else if constexpr (VEC % 2 == 0) {
+#pragma unroll
+      for (int e = 0; e < NP; ++e) *reinterpret_cast<unsigned long long*>(dst + 2 * e) = p[e];
     } else {
       *dst = __uint_as_float((unsigned)p[0]);
     }

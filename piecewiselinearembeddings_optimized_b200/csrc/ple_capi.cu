@@ -219,6 +219,13 @@ size_t ple_backward_workspace_size(int64_t batch, int64_t n_features, int64_t ma
   return b ? b : 16;
 }
 
+int ple_backward_kernel_kind(int64_t n_features, int64_t max_n_bins, int64_t d_embedding) {
+  const int rc = check_sizes(1, n_features, max_n_bins, d_embedding, kWideMaxBins);
+  if (rc != PLE_OK) return -rc;
+  if (max_n_bins > 256) return PLE_BACKWARD_WIDE;
+  return backward_uses_hist(n_features, max_n_bins, d_embedding) ? PLE_BACKWARD_HISTOGRAM : PLE_BACKWARD_SORTED;
+}
+
 static int backward_impl(const void* g, int grad_dtype, const float* x, const float* edges, const float* inv_w,
                          const int32_t* n_bins, const float* W, const float* bias, const float* w0,
                          const float* b0, int epi, int relu, int compute_dtype, int64_t N, int64_t F,

@@ -120,6 +120,7 @@ size_t wide_workspace_bytes(int64_t F, int64_t B, int64_t D);
 int launch_backward(BwdArgs a, int compute_dtype, int grad_dtype, int vec, cudaStream_t st);
 int backward_vec(int64_t D, int grad_bytes);
 size_t backward_workspace_bytes(int64_t N, int64_t F, int64_t B, int64_t D);
+bool backward_uses_hist(int64_t F, int64_t B, int64_t D);
 int launch_linear(const LinearCall& c, cudaStream_t st);
 size_t linear_workspace_bytes(int64_t F, int64_t B, int64_t D, int64_t H, int compute_dtype);
 int linear_status();

@@ -86,6 +86,44 @@ __device__ __forceinline__ void round2(float& lo, float& hi) {
   if constexpr (!std::is_same<T, float>::value) widen_pack<T>(cvt_pack<T>(lo, hi), lo, hi);
 }
 
+// ---------------------------------------------------------------- shared memory
+// 32-bit shared-window address of a pointer into dynamic shared memory.
+__device__ __forceinline__ uint32_t shared_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// n packed fp32 pairs at a shared address (16-byte accesses where n is even and `wide`): plain loads for
+// tables that do not change while they are read; ordered (volatile) loads and stores for sums that the
+// same warp updates in place.
+template <int N, bool WIDE>
+__device__ __forceinline__ void lds_pairs(unsigned long long (&v)[N], uint32_t addr) {
+#pragma unroll
+  for (int e = 0; e < N; e += (WIDE ? 2 : 1)) {
+    if constexpr (WIDE) asm("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v[e]), "=l"(v[e + 1]) : "r"(addr + 8 * e));
+    else asm("ld.shared.b64 %0, [%1];" : "=l"(v[e]) : "r"(addr + 8 * e));
+  }
+}
+template <int N, bool WIDE>
+__device__ __forceinline__ void lds_pairs_ordered(unsigned long long (&v)[N], uint32_t addr) {
+#pragma unroll
+  for (int e = 0; e < N; e += (WIDE ? 2 : 1)) {
+    if constexpr (WIDE)
+      asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(v[e]), "=l"(v[e + 1]) : "r"(addr + 8 * e) : "memory");
+    else asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v[e]) : "r"(addr + 8 * e) : "memory");
+  }
+}
+template <int N, bool WIDE>
+__device__ __forceinline__ void sts_pairs_ordered(uint32_t addr, const unsigned long long (&v)[N]) {
+#pragma unroll
+  for (int e = 0; e < N; e += (WIDE ? 2 : 1)) {
+    if constexpr (WIDE)
+      asm volatile("st.shared.v2.b64 [%0], {%1, %2};" ::"r"(addr + 8 * e), "l"(v[e]), "l"(v[e + 1]) : "memory");
+    else asm volatile("st.shared.b64 [%0], %1;" ::"r"(addr + 8 * e), "l"(v[e]) : "memory");
+  }
+}
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- cp.async
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));

@@ -41,6 +41,25 @@ def test_abi_version_and_status_strings():
     assert lib.ple_status_string(99) == b"unknown status"
 
 
+def test_backward_kernel_kind_without_a_device():
+    """Kernel choice from the sizes alone (B200 defaults when no device is visible): the histogram kernel for
+    d_embedding 8 / 16 / 24 up to 256 bins, the sorted kernel for other widths, the wide kernels above 256 bins,
+    a negative status for refused sizes."""
+    import os
+
+    lib = _native.capi()
+    hist = 0 if os.environ.get("PLE_BACKWARD_KERNEL") == "sorted" else 1
+    assert lib.ple_backward_kernel_kind(512, 64, 16) == hist
+    assert lib.ple_backward_kernel_kind(256, 32, 24) == hist
+    assert lib.ple_backward_kernel_kind(8, 16, 8) == hist
+    assert lib.ple_backward_kernel_kind(512, 64, 32) == 0
+    assert lib.ple_backward_kernel_kind(128, 64, 64) == 0
+    assert lib.ple_backward_kernel_kind(3, 10, 15) == 0
+    assert lib.ple_backward_kernel_kind(4, 1000, 16) == 2
+    assert lib.ple_backward_kernel_kind(0, 16, 16) < 0
+    assert lib.ple_backward_kernel_kind(4, 16, 0) < 0
+
+
 FAKE = None  # placeholder pointer for calls refused before any launch (set per test)
 
 

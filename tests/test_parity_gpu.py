@@ -7,6 +7,9 @@ mode rtol 1e-2 (atol 1e-2; gradients 2e-2).  Every call goes through the
 """
 from __future__ import annotations
 
+import os
+import subprocess
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -88,7 +91,7 @@ def check_grads(res, ref, abs_sums, low):
 @pytest.mark.parametrize("case", cases.BIN_CASES)
 @pytest.mark.parametrize("version", ["A", "B"])
 @pytest.mark.parametrize("relu", [False, True])
-@pytest.mark.parametrize("d", [10, 15, 20, 24])
+@pytest.mark.parametrize("d", [8, 10, 15, 16, 20, 24])
 def test_fused_fp32_matches_oracle(ops, cuda_device, case, version, relu, d):
     bins = cases.make_bins(case)
     x = cases.sample_x(bins, 128, 1000 + d, integer=(case == "ties"))
@@ -387,3 +390,35 @@ def test_full_size_properties(ops, cuda_device, name):
     for a_, f_, b_ in zip(acc, full[1:], bounds):
         if f_.numel():
             o.assert_reduction_close(a_.cpu().numpy(), f_.cpu().numpy(), 2 * b_.cpu().numpy(), err_msg="shards")
+
+
+# ---------------------------------------------------------------- the two fused backward kernels
+
+def test_backward_kernel_kind(cuda_device):
+    """D = 8 / 16 / 24 run the histogram kernel unless PLE_BACKWARD_KERNEL=sorted; other widths the sorted one."""
+    from piecewiselinearembeddings_optimized_b200 import _native
+
+    lib = _native.capi()
+    sorted_only = os.environ.get("PLE_BACKWARD_KERNEL") == "sorted"
+    for d in (8, 16, 24):
+        assert lib.ple_backward_kernel_kind(512, 64, d) == (0 if sorted_only else 1), d
+    for d in (4, 10, 32, 64):
+        assert lib.ple_backward_kernel_kind(512, 64, d) == 0, d
+    assert lib.ple_backward_kernel_kind(8, 300, 16) == 2
+
+
+def test_sorted_backward_kernel_matches_oracle(cuda_device):
+    """The sorted kernel on the shapes the histogram kernel takes by default (so that both stay checked):
+    the configuration, low-precision and determinism cases again in a child process with
+    PLE_BACKWARD_KERNEL=sorted."""
+    if os.environ.get("PLE_BACKWARD_KERNEL") == "sorted":
+        pytest.skip("already the sorted kernel")
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, PLE_BACKWARD_KERNEL="sorted")
+    sel = ("test_configs_match_oracle or test_fused_low_precision_matches_oracle or "
+           "test_backward_is_bitwise_deterministic or test_backward_kernel_kind")
+    r = subprocess.run([sys.executable, "-m", "pytest", str(Path(__file__)), "-q", "-x", "-m", "gpu",
+                        "-p", "no:cacheprovider", "-k", sel], cwd=root, env=env, capture_output=True, text=True,
+                       timeout=1800)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+
