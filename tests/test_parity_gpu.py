@@ -395,13 +395,16 @@ def test_full_size_properties(ops, cuda_device, name):
 # ---------------------------------------------------------------- the two fused backward kernels
 
 def test_backward_kernel_kind(cuda_device):
-    """D = 8 / 16 / 24 run the histogram kernel unless PLE_BACKWARD_KERNEL=sorted; other widths the sorted one."""
+    """D = 8 / 16 / 24 run the histogram kernel where its private sums fit in shared memory (unless
+    PLE_BACKWARD_KERNEL=sorted); other widths, and D = 24 with 64 bins (16 warps x 64 x 24 x 2 floats of sums
+    alone take 192 KB), the sorted one."""
     from piecewiselinearembeddings_optimized_b200 import _native
 
     lib = _native.capi()
     sorted_only = os.environ.get("PLE_BACKWARD_KERNEL") == "sorted"
-    for d in (8, 16, 24):
-        assert lib.ple_backward_kernel_kind(512, 64, d) == (0 if sorted_only else 1), d
+    for f, b, d in ((512, 64, 8), (512, 64, 16), (256, 32, 24)):
+        assert lib.ple_backward_kernel_kind(f, b, d) == (0 if sorted_only else 1), d
+    assert lib.ple_backward_kernel_kind(512, 64, 24) == 0
     for d in (4, 10, 32, 64):
         assert lib.ple_backward_kernel_kind(512, 64, d) == 0, d
     assert lib.ple_backward_kernel_kind(8, 300, 16) == 2
