@@ -79,13 +79,17 @@ int ple_abi_version(void);
 const char* ple_status_string(int status);
 
 /*
- * Backward kernel.  ple_backward and ple_embeddings_backward (and the
- * no-allocation variant) run one kernel: per tile of samples a counting sort
- * of each feature's samples by bin, then a segmented walk over the sorted
- * lists that keeps each run's gradient sums in registers; the parameter
- * gradients are summed per partition in the workspace and reduced in a fixed
- * order, so every result is bitwise deterministic for a given shape and
- * device.
+ * Backward kernels.  ple_backward and ple_embeddings_backward (and the
+ * no-allocation variant) run one of two fused kernels up to 256 bins
+ * (ple_backward_kernel_kind tells which): the histogram kernel (samples in
+ * natural order, per-warp bin sums in shared memory updated in sample order;
+ * d_embedding 8, 16 or 24) or the sorted kernel (per tile of samples a
+ * counting sort of each feature's samples by bin, then a segmented walk over
+ * the sorted lists that keeps each run's gradient sums in registers).  Either
+ * way the parameter gradients are summed per partition in the workspace and
+ * reduced in a fixed order, so every result is bitwise deterministic for a
+ * given shape and device.  Above 256 bins the bare x_ple backward sums
+ * grad_weight with atomics (not bitwise reproducible).
  */
 
 /* Detail message of the last failing call on the calling host thread. */

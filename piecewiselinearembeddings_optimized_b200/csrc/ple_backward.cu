@@ -135,8 +135,8 @@ static size_t ws_bytes_for(const BwdArgs& a, int grid) {
 }
 
 // Histogram kernel: D = 4 VEC with VEC in {2, 4, 6}, at most 256 bins; features per CTA (4, 2, 1, preferred
-// in that order: whole 16-byte x / grad_x pieces per sample) and the longest tile (an even number of
-// 32-sample batches per warp) whose layout fits.
+// in that order: whole 16-byte x / grad_x pieces per sample) and the longest tile (2 to 16 batches of 32
+// samples per warp) whose layout fits.
 static bool hist_plan(BwdArgs& a, size_t* smem_out) {
   const int vec = a.D / kHistNC;
   if (a.D % kHistNC != 0 || (vec != 2 && vec != 4 && vec != 6) || a.B > 256 || a.B < 1) return false;
@@ -145,15 +145,14 @@ static bool hist_plan(BwdArgs& a, size_t* smem_out) {
   const size_t optin = device_max_smem_optin();
   for (int lgFc = 2; lgFc >= 0; --lgFc) {
     if (lgFc > 0 && (1 << (lgFc - 1)) >= a.F) continue;
-    const int Fc = 1 << lgFc, Wf = kBwdWarps / Fc;
-    for (int lgSt = 9; (1 << lgSt) >= 64 * Wf; --lgSt) {  // an even number of 32-sample batches per warp
-      const size_t bytes = hist_layout_bytes(a.B, a.D, Fc, 1 << lgSt, 1 << a.lgk, nullptr, nullptr);
+    const int Fc = 1 << lgFc, Wf = kHistWarps / Fc;
+    for (int batches = 16; batches >= 2; batches /= 2) {  // batches per warp per tile
+      const int St = 32 * Wf * batches;
+      const size_t bytes = hist_layout_bytes(a.B, a.D, Fc, St, 1 << a.lgk, nullptr, nullptr);
       if (bytes > optin) continue;
       a.lgFc = lgFc;
       a.Fc = Fc;
-      a.lgWf = 0;
-      while ((1 << a.lgWf) < Wf) ++a.lgWf;
-      a.lgSt = lgSt;
+      a.hist_St = St;
       a.n_chunks = (int)ceil_div<int64_t>(a.F, Fc);
       *smem_out = bytes;
       return true;

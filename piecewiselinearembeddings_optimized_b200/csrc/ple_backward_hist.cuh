@@ -5,31 +5,40 @@
 // backward_cuda.cu:343-492 for grad_x, :268-336 for grad_W):
 //   H[j] = sum_{b: k_b = j} q(g'_b),  U[j] = sum_{b: k_b = j} q(t_b) q(g'_b),
 //   grad_W[phys(j)] = U[j] + sum_{j' > j} H[j'],
-//   grad_x = <q(g'), Q[k]> (+ <q(g'), Q[k - 1]> at an interior edge tie)
-//            (+ <g, w0> for epilogue B),  Q[k] = r_k S[k].
+//   grad_x = r_k <q(g'), S[k]> (+ r_{k-1} <q(g'), S[k - 1]> at an interior edge tie)
+//            (+ <g, w0> for epilogue B).
 //
 // Work decomposition.  One persistent CTA of 16 warps per SM; chunks of Fc
 // features, slots of `group` CTAs over the same sample ranges and the
 // workspace blocks are those of the sorted kernel (the finalize is shared).
-// A chunk's warps split evenly over its features (Wf = 16 / Fc per feature).
-// Each warp owns a private copy of its feature's H / U sums ([B][4][2 VEC]
-// floats: lane chunk c of bin k holds H[c VEC ..] then U[c VEC ..]), so no
-// two warps ever write the same word.  Per tile of S_t samples (x arrives by
-// cp.async one tile ahead, the next tile's gradient rows are prefetched into
-// L2 by one tensor-map instruction per 256 rows) each warp takes batches of
-// 32 samples of its feature, interleaved with the feature's other warps:
-//   * search: one sample per lane (the forward's bin indices when given,
-//     else an L-level descent over the interior edges in breadth-first
-//     order), q(t), the tie flag;
-//   * 4 steps of 8 samples, 4 lanes x VEC elements per D row: the gradient
-//     chunk (loaded one batch ahead), the ReLU mask (skipped, bit-identically,
-//     when every sample of the step is in an "open" bin, one whose ReLU input
-//     is positive for every t the bin admits), grad_x shares (summed over the
-//     row's 4 lanes by shuffles), the epilogue sums, then H += q(g'),
-//     U += q(t) q(g') into the warp's copy.  Samples of one step that share a
-//     bin (found by match.any) update it in rounds, in sample order.  Lanes
-//     of odd samples read and write the U half of a chunk before the H half,
-//     so the two samples of a quarter-warp never meet in a bank.
+// A chunk's warps split evenly over its features (Wf = 16 / Fc per feature)
+// and each warp owns a private copy of its feature's H / U sums, so no two
+// warps ever write the same word.  A D row is 4 lanes x VEC elements; a warp
+// step is 8 samples (rows).  Per tile of S_t samples (x arrives by cp.async
+// one tile ahead, the next tile's gradient rows are prefetched into L2 by one
+// tensor-map instruction per 256 rows) each warp takes batches of 32 samples
+// of its feature, interleaved with the feature's other warps:
+//   * search: one sample per lane (the forward's bin indices when given, else
+//     an L-level descent over the interior edges in breadth-first order); the
+//     sample's record {bin row offset | flags, q(t), x, r_k} goes to the
+//     warp's record buffer;
+//   * 4 steps of 8 samples: each lane reads its row's record (one 16-byte
+//     load, shared by the row's 4 lanes), the S / T units of the sample's bin,
+//     computes q(g') (the ReLU mask; skipped, bit-identically, when every
+//     sample of the step is in an "open" bin, one whose ReLU input is positive
+//     for every t it admits), the epilogue sums, its share of grad_x (summed
+//     over the row's 4 lanes by shuffles);
+//   * then, step by step, H += q(g'), U += q(t) q(g') into the warp's copy
+//     (one predicated 16-byte read-modify-write per element pair).  Samples of
+//     one step that share a bin (found by match.any) update it in rounds, in
+//     sample order.
+// Shared-memory layout: every bin row of the S / T table and of the H / U sums
+// is a sequence of 16-byte units, one per element pair ({S_2m, S_2m+1,
+// T_2m, T_2m+1}, {H_2m, H_2m+1, U_2m, U_2m+1}), lane c owning units
+// c NP .. c NP + NP - 1 (NP = VEC / 2).  With NP = 2 (D = 16) a bin row is 128
+// bytes and the lanes of odd rows take their two units in the opposite order
+// (their gradient pairs swapped to match), so the two rows that share a
+// 128-byte wavefront read disjoint bank groups whatever their bins.
 // At the end of a segment the Wf copies of a feature are summed in warp order,
 // a suffix scan over bins turns H / U into grad_W and the partial goes to the
 // workspace.  No floating-point atomics: bitwise deterministic for a given
@@ -41,14 +50,20 @@
 namespace ple {
 
 constexpr int kHistNC = 4;  // lanes per D row: 8 samples per warp step, 4 steps per batch of 32
+// 16 warps per CTA (128 registers a thread; measured faster than 12 warps with 168 registers)
+constexpr int kHistWarps = 16, kHistThreads = 32 * kHistWarps;
+
+// record flags (low bits of the bin row offset, which is a multiple of 64): tie, open bin, dead row, and the
+// sample's rank among the samples of its step that share its bin (bits 3-5)
+constexpr int kRecTie = 1, kRecOpen = 2, kRecDead = 4, kRecRankShift = 3, kRecRank = 7 << kRecRankShift;
+constexpr int kRecFlags = 63;
 
 struct HistLayout {
-  float* sAcc;      // [16 warps][B][kHistNC][2 VEC] private H / U sums
-  float* sQ;        // [Fc][B][2][D] Q = r_k S_k, twice per bin (odd samples read the second copy)
-  float* sS;        // [Fc][B][D] S = q(W) in logical bin order (masked path)
-  float* sT;        // [Fc][B][D] exclusive prefix of S (masked path)
-  float* sX;        // [2][Fc][S_t] x tiles (transposed)
+  float* sAcc;      // [16 warps][B][2 D] private H / U units
+  float* sST;       // [Fc][B][2 D] S / T units, logical bin order
+  float* sX;        // [2][Fc][S_t + 8] x tiles (transposed; the pad spreads the cp.async stores over banks)
   float* sGX;       // [2][S_t][Fc] grad_x tiles
+  float4* sRec;     // [16 warps][32] sample records of the current batch
   float* sKey;      // [Fc][nkeys] interior edges in breadth-first order (node 1 = root)
   float2* sER;      // [Fc][B] {e_k, r_k}
   unsigned* sOpen;  // [Fc][ceil(B / 32)] open-bin bits
@@ -56,22 +71,23 @@ struct HistLayout {
   int* sN;          // [Fc] real bins per feature
 };
 
+__host__ __device__ __forceinline__ int hist_xld(int S_t) { return S_t + 8; }
+
 __host__ __device__ __forceinline__ size_t hist_layout_bytes(int B, int D, int Fc, int S_t, int nkeys, HistLayout* L,
                                                              unsigned char* base) {
-  const int Wf = kBwdWarps / Fc;
+  const int Wf = kHistWarps / Fc;
   const int ow = (B + 31) / 32;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     size_t o = off;
-    off += (bytes + 15) & ~(size_t)15;
+    off += (bytes + 127) & ~(size_t)127;  // 128-byte aligned: bin rows start on a bank-window boundary
     return base + o;
   };
-  unsigned char* pAcc = take((size_t)kBwdWarps * B * D * 2 * 4);
-  unsigned char* pQ = take((size_t)Fc * B * 2 * D * 4);
-  unsigned char* pS = take((size_t)Fc * B * D * 4);
-  unsigned char* pT = take((size_t)Fc * B * D * 4);
-  unsigned char* pX = take((size_t)2 * Fc * S_t * 4);
+  unsigned char* pAcc = take((size_t)kHistWarps * B * D * 2 * 4);
+  unsigned char* pST = take((size_t)Fc * B * D * 2 * 4);
+  unsigned char* pX = take((size_t)2 * Fc * hist_xld(S_t) * 4);
   unsigned char* pGX = take((size_t)2 * S_t * Fc * 4);
+  unsigned char* pRec = take((size_t)kHistWarps * 32 * 16);
   unsigned char* pK = take((size_t)Fc * nkeys * 4);
   unsigned char* pER = take((size_t)Fc * B * 8);
   unsigned char* pO = take((size_t)Fc * ow * 4);
@@ -79,11 +95,10 @@ __host__ __device__ __forceinline__ size_t hist_layout_bytes(int B, int D, int F
   unsigned char* pN = take((size_t)Fc * 4);
   if (L) {
     L->sAcc = reinterpret_cast<float*>(pAcc);
-    L->sQ = reinterpret_cast<float*>(pQ);
-    L->sS = reinterpret_cast<float*>(pS);
-    L->sT = reinterpret_cast<float*>(pT);
+    L->sST = reinterpret_cast<float*>(pST);
     L->sX = reinterpret_cast<float*>(pX);
     L->sGX = reinterpret_cast<float*>(pGX);
+    L->sRec = reinterpret_cast<float4*>(pRec);
     L->sKey = reinterpret_cast<float*>(pK);
     L->sER = reinterpret_cast<float2*>(pER);
     L->sOpen = reinterpret_cast<unsigned*>(pO);
@@ -93,12 +108,20 @@ __host__ __device__ __forceinline__ size_t hist_layout_bytes(int B, int D, int F
   return off;
 }
 
-// The chunk's tables for one segment and zeroed private sums: search keys, {e_k, r_k}, S = q(W) in
-// logical bin order, its exclusive prefix T, Q = r S (twice per bin), the open bits.
-template <typename QT, int MASK>
+// Float offset of element d inside a bin row of 16-byte pair units (S or H at +0, T or U at +2).
+template <int VEC>
+__device__ __forceinline__ int unit_float(int d) {
+  constexpr int NP = VEC / 2;
+  const int c = d / VEC, e = d - c * VEC;
+  return (c * NP + (e >> 1)) * 4 + (e & 1);
+}
+
+// The chunk's tables for one segment and zeroed private sums: search keys, {e_k, r_k}, S = q(W) and its
+// exclusive prefix T in logical bin order (pair units), the open bits.
+template <typename QT, int MASK, int VEC>
 __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLayout& L, int f0, int fc, int Fc,
-                                                  int D, int nkeys, int lgk, int tid, int nthr) {
-  const int B = a.B;
+                                                  int nkeys, int lgk, int tid, int nthr) {
+  const int B = a.B, D = a.D, D2 = 2 * D;
   const int ow = (B + 31) / 32;
   for (int i = tid; i < Fc; i += nthr) {
     const int n = i < fc ? a.n_bins[f0 + i] : 1;
@@ -106,9 +129,10 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
   }
   {
     float4* acc = reinterpret_cast<float4*>(L.sAcc);
-    const int n4 = kBwdWarps * B * D * 2 / 4;
+    const int n4 = kHistWarps * B * D2 / 4;
     for (int idx = tid; idx < n4; idx += nthr) acc[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int idx = tid; idx < Fc * B * D; idx += nthr) L.sS[idx] = 0.0f;
+    float4* st = reinterpret_cast<float4*>(L.sST);
+    for (int idx = tid; idx < Fc * B * D2 / 4; idx += nthr) st[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
   for (int idx = tid; idx < Fc * nkeys; idx += nthr) {
@@ -130,30 +154,25 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
     }
     L.sER[idx] = make_float2(e, r);
   }
+  // S[i][logical bin] = q(W[i][physical bin]); one thread per (row, element)
   const float* Wc = a.W + (int64_t)f0 * B * D;
-  for (int row = tid; row < fc * B; row += nthr) {
+  for (int idx = tid; idx < fc * B * D; idx += nthr) {
+    const int row = idx / D, d = idx - row * D;
     const int i = row / B, p = row - i * B;
     const int n = L.sN[i];
     const int lg = (p == B - 1) ? n - 1 : (p < n - 1 ? p : -1);
-    if (lg >= 0) {
-      const float* src = Wc + (int64_t)row * D;
-      float* dst = L.sS + (i * B + lg) * D;
-      for (int d = 0; d < D; ++d) dst[d] = quantize<QT>(src[d]);
-    }
+    if (lg >= 0) L.sST[(i * B + lg) * D2 + unit_float<VEC>(d)] = quantize<QT>(Wc[idx]);
   }
   __syncthreads();
   for (int col = tid; col < Fc * D; col += nthr) {
     const int i = col / D, d = col - i * D;
     const int n = L.sN[i];
+    const int uo = unit_float<VEC>(d);
     float acc = 0.0f;
-    for (int j = 0; j < B; ++j) {
-      const int o = (i * B + j) * D + d;
-      const float S = L.sS[o];
-      L.sT[o] = j < n ? acc : 0.0f;
-      acc += j < n ? S : 0.0f;
-      const float q = S * L.sER[i * B + j].y;
-      L.sQ[(2 * (i * B + j)) * D + d] = q;
-      L.sQ[(2 * (i * B + j) + 1) * D + d] = q;
+    for (int j = 0; j < n; ++j) {
+      float* u = L.sST + (i * B + j) * D2 + uo;
+      u[2] = acc;
+      acc += u[0];
     }
   }
   __syncthreads();
@@ -171,7 +190,8 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
         const float tmax = last ? 0.0f : quantize<QT>((a.edges[(int64_t)(f0 + i) * (B + 1) + k + 1] - er.x) * er.y);
         open = true;
         for (int d = 0; d < D && open; ++d) {
-          const float S = L.sS[(i * B + k) * D + d], T = L.sT[(i * B + k) * D + d];
+          const float* u = L.sST + (i * B + k) * D2 + unit_float<VEC>(d);
+          const float S = u[0], T = u[2];
           const float bias = MASK == kMaskReluBias ? a.bias[(int64_t)(f0 + i) * D + d] : 0.0f;
           const float p0 = fmaf(0.0f, S, T), p1 = fmaf(tmax, S, T);
           if (p0 != p0 || p1 != p1 || !relu_passes<QT, MASK>(p0, bias) || !relu_passes<QT, MASK>(p1, bias))
@@ -185,10 +205,6 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
   }
   __syncthreads();
 }
-
-// Step word of a sample: bin in bits 0-7, then the flags; dead lanes (past the tile) carry their lane in
-// bits 12-16 so that no two of them match.
-constexpr int kTieBit = 1 << 8, kOpenBit = 1 << 9, kDeadBit = 1 << 10;
 
 // Count of interior edges e_1 .. e_{2^L - 1} (breadth-first in keys[1 ..]) with !(x < e): the L-level
 // descent, unrolled per level count.
@@ -212,98 +228,141 @@ __device__ __forceinline__ int hist_search(const float* keys, float x, int lgk) 
   }
 }
 
-// One step of one lane: q(g') of its VEC elements (the ReLU mask on the EXACT path only: every sample
-// of the step in an open bin makes it a no-op), the epilogue sums, and the lane's share of grad_x
-// (<q(g'), Q[k]>, plus <g, w0> for epilogue B).  Same arithmetic as walk_step of the sorted kernel.
-template <typename QT, typename GT, int VEC, int MASK, int EPIV, bool EXACT>
-__device__ __forceinline__ float hist_body(const GRaw<GT, VEC>& g, float tv, float xv, const Row<VEC>& Qr,
-                                           uint32_t st_addr, uint32_t tt_addr, const Row<VEC>& pbias,
-                                           const Row<VEC>& w0r, Row<VEC>& aw, Row<VEC>& ab,
-                                           f2_t (&qv)[Row<VEC>::NP]) {
-  constexpr int NP = Row<VEC>::NP;
-  constexpr bool LIN = EPIV == kEpvLin;
-  constexpr bool ROUND_G = !std::is_same<GT, QT>::value && !std::is_same<QT, float>::value;
-  constexpr bool WIDE = VEC % 4 == 0;
-  const float thr = zero_round_threshold<QT>();
-  const f2_t t2 = pack2(tv, tv);
-  f2_t Sk[NP], Tk[NP];
-  if constexpr (EXACT && MASK != kMaskNone) {
-    lds_pairs<NP, WIDE>(Sk, st_addr);
-    lds_pairs<NP, WIDE>(Tk, tt_addr);
+// ---------------------------------------------------------------- shared-memory access of pair units
+__device__ __forceinline__ float4 lds_rec(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts_rec(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// {first pair, second pair} of a table unit (tables do not change while a tile is walked)
+__device__ __forceinline__ void lds_unit(uint32_t addr, f2_t& a, f2_t& b) {
+  asm("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+
+// Unit u of a lane's NP units, given the address of its first one; with NP == 2 the lane's first unit is
+// the one its row parity reads first and the second is d1 = +16 or -16 bytes away.
+template <int NP>
+__device__ __forceinline__ uint32_t unit_addr(uint32_t a0, int u, uint32_t d1) {
+  if constexpr (NP == 2) return u == 0 ? a0 : a0 + d1;
+  else return a0 + 16u * u;
+}
+
+// H += g', U += t g' for the lane's NP units of one sample, when `live` (predicated, no branch).
+template <int NP>
+__device__ __forceinline__ void hist_rmw(uint32_t live, uint32_t a0, uint32_t d1, const f2_t (&g)[NP], f2_t t2) {
+  if constexpr (NP == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
+        "@p add.rn.f32x2 h0, h0, %2;\n\t"
+        "@p fma.rn.f32x2 u0, %3, %2, u0;\n\t"
+        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t}" ::"r"(live),
+        "r"(a0), "l"(g[0]), "l"(t2)
+        : "memory");
+  } else if constexpr (NP == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0, h1, u1;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
+        "@p ld.shared.v2.b64 {h1, u1}, [%2];\n\t"
+        "@p add.rn.f32x2 h0, h0, %3;\n\t"
+        "@p fma.rn.f32x2 u0, %5, %3, u0;\n\t"
+        "@p add.rn.f32x2 h1, h1, %4;\n\t"
+        "@p fma.rn.f32x2 u1, %5, %4, u1;\n\t"
+        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t"
+        "@p st.shared.v2.b64 [%2], {h1, u1};\n\t}" ::"r"(live),
+        "r"(a0), "r"(unit_addr<2>(a0, 1, d1)), "l"(g[0]), "l"(g[1]), "l"(t2)
+        : "memory");
+  } else {
+    static_assert(NP == 3, "pair units per lane: 1, 2 or 3");
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0, h1, u1, h2, u2;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
+        "@p ld.shared.v2.b64 {h1, u1}, [%1+16];\n\t"
+        "@p ld.shared.v2.b64 {h2, u2}, [%1+32];\n\t"
+        "@p add.rn.f32x2 h0, h0, %2;\n\t"
+        "@p fma.rn.f32x2 u0, %5, %2, u0;\n\t"
+        "@p add.rn.f32x2 h1, h1, %3;\n\t"
+        "@p fma.rn.f32x2 u1, %5, %3, u1;\n\t"
+        "@p add.rn.f32x2 h2, h2, %4;\n\t"
+        "@p fma.rn.f32x2 u2, %5, %4, u2;\n\t"
+        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t"
+        "@p st.shared.v2.b64 [%1+16], {h1, u1};\n\t"
+        "@p st.shared.v2.b64 [%1+32], {h2, u2};\n\t}" ::"r"(live),
+        "r"(a0), "l"(g[0]), "l"(g[1]), "l"(g[2]), "l"(t2)
+        : "memory");
   }
-  f2_t d2 = 0ull, dw2 = 0ull;
-  f2_t x2 = 0ull;
-  if constexpr (LIN) x2 = pack2(xv, xv);
+}
+
+// Rounds 1, 2, ... of the ordered read-modify-writes of one step whose samples share a bin (kept out of
+// line: inlined, the rounds raised the register pressure of the whole loop into spills).
+template <int NP>
+__device__ __noinline__ void hist_rmw_rounds(uint32_t live, int rank, uint32_t a0, uint32_t d1, f2_t q0, f2_t q1,
+                                             f2_t q2, f2_t t2) {
+  f2_t q[NP];
+  q[0] = q0;
+  if constexpr (NP > 1) q[1] = q1;
+  if constexpr (NP > 2) q[2] = q2;
+  for (int rd = 1;; ++rd) {
+    __syncwarp();
+    hist_rmw<NP>(live && rank == rd ? 1u : 0u, a0, d1, q, t2);
+    if (!__any_sync(0xffffffffu, rank > rd)) break;
+  }
+}
+template <int NP>
+__device__ __forceinline__ void hist_rmw_rounds(uint32_t live, int rank, uint32_t a0, uint32_t d1,
+                                                const f2_t (&q)[NP], f2_t t2) {
+  hist_rmw_rounds<NP>(live, rank, a0, d1, q[0], NP > 1 ? q[NP > 1 ? 1 : 0] : 0ull, NP > 2 ? q[NP > 2 ? 2 : 0] : 0ull,
+                      t2);
+}
+
+// The lane's NP gradient pairs of one sample in unit order (NP == 2 and an odd row: swapped).
+template <typename GT, int VEC>
+__device__ __forceinline__ void grad_pairs(const GRaw<GT, VEC>& g, bool swap, f2_t (&out)[VEC / 2]) {
+  constexpr int NP = VEC / 2;
 #pragma unroll
-  for (int e = 0; e < NP; ++e) {
-    const f2_t g2 = raw_pair<GT, VEC>(g, e);
-    if constexpr (LIN) {
-      dw2 = fma2(g2, w0r.p[e], dw2);
-      aw.p[e] = fma2(g2, x2, aw.p[e]);
-      ab.p[e] = add2(ab.p[e], g2);
-    }
-    f2_t qq = g2;
-    if constexpr (EXACT && MASK != kMaskNone) {
-      float p0, p1, g0, g1;
-      unpack2(fma2(t2, Sk[e], Tk[e]), p0, p1);
-      unpack2(g2, g0, g1);
-      if constexpr (MASK == kMaskReluBias) {
-        round2<QT>(p0, p1);
-        float b0, b1;
-        unpack2(pbias.p[e], b0, b1);
-        p0 += b0;
-        p1 += b1;
-        qq = pack2(p0 <= 0.f ? 0.f : g0, p1 <= 0.f ? 0.f : g1);
-      } else {
-        qq = pack2(p0 <= thr ? 0.f : g0, p1 <= thr ? 0.f : g1);
-      }
-    }
-    if constexpr (EPIV == kEpvBias) aw.p[e] = add2(aw.p[e], qq);  // sum g' (before the QT rounding)
-    if constexpr (ROUND_G) {
-      float q0, q1;
-      unpack2(qq, q0, q1);
-      round2<QT>(q0, q1);
-      qq = pack2(q0, q1);
-    }
-    qv[e] = qq;
-    d2 = fma2(qq, Qr.p[e], d2);
+  for (int e = 0; e < NP; ++e) out[e] = raw_pair<GT, VEC>(g, e);
+  if constexpr (NP == 2) {
+    const f2_t p0 = out[0], p1 = out[1];
+    out[0] = swap ? p1 : p0;
+    out[1] = swap ? p0 : p1;
   }
-  float lo, hi;
-  unpack2(d2, lo, hi);
-  float gx = lo + hi;
-  if constexpr (LIN) {
-    unpack2(dw2, lo, hi);
-    gx += lo + hi;
-  }
-  return gx;
 }
 
 template <typename QT, typename GT, int VEC, int MASK, int EPIV>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kHistThreads, 1)
     ple_bwd_hist_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap gmap) {
   constexpr int NC = kHistNC, R = 32 / NC, J = NC;  // lanes per row, samples per step, steps per batch
+  // steps processed together (registers: a group's records, units and sums are live together)
+  constexpr int JG = VEC == 6 ? 1 : 2;
+  constexpr int NG = J / JG;  // groups per batch (even)
   constexpr int D = NC * VEC;
-  constexpr int CH = 2 * VEC;  // floats of one lane chunk of a bin row (H, then U)
-  constexpr int NP = Row<VEC>::NP;
+  constexpr int NP = VEC / 2;
   constexpr bool LIN = EPIV == kEpvLin;
   constexpr bool ACC = EPIV != kEpvNone;
-  constexpr bool WIDE = VEC % 4 == 0;
-  constexpr uint32_t kRow = 2 * D * 4;  // bytes of a Q row and of a bin row of the sums
-  static_assert(VEC >= 2 && VEC % 2 == 0, "the histogram kernel packs fp32 pairs");
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr bool ROUND_G = !std::is_same<GT, QT>::value && !std::is_same<QT, float>::value;
+  constexpr uint32_t kRow = 2 * D * 4;  // bytes of a bin row (S / T units, H / U units)
+  static_assert(VEC == 2 || VEC == 4 || VEC == 6, "the histogram kernel packs 1 to 3 fp32 pairs per lane");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const int B = a.B;
-  const int Fc = a.Fc, S_t = 1 << a.lgSt;
-  const int Wf = kBwdWarps / Fc;
+  const int Fc = a.Fc, S_t = a.hist_St;
+  const int Wf = kHistWarps / Fc;
   const int nkeys = 1 << a.lgk;
   const int ow = (B + 31) / 32;
-  const int BD2 = B * D * 2;
+  const int xld = hist_xld(S_t);
   HistLayout L;
   hist_layout_bytes(B, D, Fc, S_t, nkeys, &L, smem_raw);
 
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int lane = tid & 31, wid = tid >> 5;
-  const int r = lane / NC, c = lane - r * NC, cd = c * VEC;
-  const int par = r & 1;
+  const int r = lane / NC, c = lane - r * NC;
+  const bool swap = NP == 2 && (r & 1) != 0;
   const int my_i = wid / Wf, my_w = wid - my_i * Wf;
   const unsigned cmask = 0x11111111u << c;  // lanes holding chunk c of their row (NC == 4)
   const unsigned lt = (1u << lane) - 1u;
@@ -311,8 +370,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const bool do_gx = a.grad_x != nullptr;
   const GT* gptr = reinterpret_cast<const GT*>(a.g);
   const uint64_t pol_first = l2_policy_evict_first();
-  const uint64_t pol_last = l2_policy_evict_last();
-  float* acc_w = L.sAcc + (size_t)wid * BD2 + c * CH;  // this lane's chunk column of the warp's copy
+  const float thr = zero_round_threshold<QT>();
+  // this lane's first unit inside a bin row (odd rows of D = 16 start with the second pair)
+  const uint32_t lane_unit = (uint32_t)(c * NP + (swap ? 1 : 0)) * 16u;
+  const uint32_t d1 = swap ? (uint32_t)-16 : 16u;  // from the lane's first unit to its second (NP == 2)
+  const uint32_t acc_base = shared_addr(L.sAcc) + (uint32_t)wid * B * kRow + lane_unit;
+  const uint32_t rec_w = shared_addr(L.sRec + wid * 32);
+  const uint32_t rec_r = rec_w + (uint32_t)r * 16u;
 
   const int m = a.group;
   const int slot = blockIdx.x / m, member = blockIdx.x - slot * m;
@@ -336,11 +400,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     auto load_x = [&](int T) {
       const int64_t t0 = s_begin + (int64_t)T * S_t;
       const int ns = (int)min64(S_t, s_end - t0);
-      float* dst = L.sX + (T & 1) * Fc * S_t;
+      float* dst = L.sX + (T & 1) * Fc * xld;
       for (int q = tid; q < ns * Fc; q += nthr) {
         const int s = q / Fc, i = q - s * Fc;
-        if (i < fc) cp_async4(dst + i * S_t + s, a.x + (t0 + s) * a.F + f0 + i);
-        else dst[i * S_t + s] = 0.0f;
+        if (i < fc) cp_async4(dst + i * xld + s, a.x + (t0 + s) * a.F + f0 + i);
+        else dst[i * xld + s] = 0.0f;
       }
       cp_async_commit();
     };
@@ -348,6 +412,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!a.g_prefetch || tid != 0) return;
       const int64_t t0 = s_begin + (int64_t)T * S_t;
       const int ns = (int)min64(S_t, s_end - t0);
+      const uint64_t pol_last = l2_policy_evict_last();
       for (int r0 = 0; r0 < ns; r0 += 256) prefetch_tile_l2(&gmap, f0 * D, (int)(t0 + r0), pol_last);
     };
     auto store_gx = [&](int T) {
@@ -370,61 +435,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncthreads();  // previous segment finished with every shared buffer
     load_x(0);
     prefetch_g(0);
-    stage_hist_tables<QT, MASK>(a, L, f0, fc, Fc, D, nkeys, a.lgk, tid, nthr);
+    stage_hist_tables<QT, MASK, VEC>(a, L, f0, fc, Fc, nkeys, a.lgk, tid, nthr);
 
-    Row<VEC> pbias, w0r, aw, ab;  // aw: sum g x (B) or sum g' (A); ab: sum g (B)
-    pbias.zero();
-    w0r.zero();
-    aw.zero();
-    ab.zero();
-    if constexpr (MASK == kMaskReluBias) {
-      if (live_w) pbias.ldg(a.bias + (int64_t)(f0 + my_i) * D + cd);
-    }
-    if constexpr (LIN) {
-      if (live_w) w0r.ldg(a.w0 + (int64_t)(f0 + my_i) * D + cd);
+    // per-lane epilogue parameters and sums, in this lane's unit order
+    f2_t pbias[NP], w0r[NP], aw[NP], ab[NP];  // aw: sum g x (B) or sum g' (A); ab: sum g (B)
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      pbias[u] = 0ull;
+      w0r[u] = 0ull;
+      aw[u] = 0ull;
+      ab[u] = 0ull;
+      const int e0 = c * VEC + 2 * ((NP == 2 && swap) ? 1 - u : u);
+      if constexpr (MASK == kMaskReluBias) {
+        if (live_w) pbias[u] = pack2(a.bias[(int64_t)(f0 + my_i) * D + e0], a.bias[(int64_t)(f0 + my_i) * D + e0 + 1]);
+      }
+      if constexpr (LIN) {
+        if (live_w) w0r[u] = pack2(a.w0[(int64_t)(f0 + my_i) * D + e0], a.w0[(int64_t)(f0 + my_i) * D + e0 + 1]);
+      }
     }
     const float* keys = L.sKey + my_i * nkeys;
     const float2* er = L.sER + my_i * B;
     const unsigned* openw = L.sOpen + my_i * ow;
     const int n1 = L.sN[my_i] - 1;
-    // lane-constant shared-memory bases; a bin adds kofs bytes (Q and H / U rows are both 2 D floats)
-    const uint32_t qb = shared_addr(L.sQ + (my_i * B * 2 + par) * D + cd);
-    const uint32_t sb = shared_addr(L.sS + my_i * B * D + cd);
-    const uint32_t tb = shared_addr(L.sT + my_i * B * D + cd);
-    const uint32_t aA = shared_addr(acc_w + par * VEC);        // first half this lane touches
-    const uint32_t aB = shared_addr(acc_w + (par ^ 1) * VEC);  // second half
+    const uint32_t st_base = shared_addr(L.sST) + (uint32_t)my_i * B * kRow + lane_unit;
     // this lane's gradient row of step 0 of the warp's first batch; batches advance by 32 Wf samples
     const int64_t FD = (int64_t)a.F * D;
-    const GT* gp = gptr + (s_begin + 32 * my_w + r) * FD + (int64_t)(f0 + my_i) * D + cd;
+    const GT* gp = gptr + (s_begin + 32 * my_w + r) * FD + (int64_t)(f0 + my_i) * D + c * VEC;
     int64_t srem = s_end - (s_begin + 32 * my_w + r);  // step j of the next batch to load is live iff j R < srem
     const int64_t gstep = (int64_t)R * FD, gbatch = (int64_t)32 * Wf * FD;
     const bool wide = a.g_wide != 0;
 
-    auto load_batch = [&](GRaw<GT, VEC> (&g)[J]) {
+    // gradient rows of steps h JG .. h JG + JG - 1 of the warp's next batch; after the last group the batch
+    // pointer moves on
+    auto load_group = [&](GRaw<GT, VEC> (&g)[JG], int h) {
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
+      for (int jj = 0; jj < JG; ++jj) {
+        const int j = h * JG + jj;
         if (live_w && j * R < srem) {
-          ldg_raw<GT, VEC>(g[j], gp + j * gstep, wide, pol_first);
+          ldg_raw<GT, VEC>(g[jj], gp + j * gstep, wide, pol_first);
         } else {
 #pragma unroll
-          for (int w = 0; w < GRaw<GT, VEC>::kWords; ++w) g[j].w[w] = 0u;
+          for (int w = 0; w < GRaw<GT, VEC>::kWords; ++w) g[jj].w[w] = 0u;
         }
       }
-      gp += gbatch;
-      srem -= 32 * Wf;
+      if (h == NG - 1) {
+        gp += gbatch;
+        srem -= 32 * Wf;
+      }
     };
 
-    // batch jb of tile T (samples sb0 .. sb0 + 31 of the tile).  The 4 steps go phase by phase (their
-    // parameters and Q rows, their arithmetic, their grad_x, their duplicate masks, and last the ordered
-    // read-modify-writes of the sums), so that the independent work of the steps overlaps.
-    auto run_batch = [&](const GRaw<GT, VEC> (&g)[J], int T, int jb) {
+    // search of batch jb of tile T (samples 32 (my_w + Wf jb) + lane of the tile), one sample per lane: its
+    // record {bin row offset | flags, q(t), x, r_k}; returns the ballot (bit j 8 + r) of the samples with rank
+    // >= 1 among the samples of their step in their bin
+    auto search = [&](int T, int jb) -> unsigned {
       const int64_t t0 = s_begin + (int64_t)T * S_t;
       const int ns = (int)min64(S_t, s_end - t0);
-      const int sb0 = 32 * (my_w + Wf * jb);
-      const float* xs = L.sX + (T & 1) * Fc * S_t + my_i * S_t;
-      const uint32_t gxa = shared_addr(L.sGX + (T & 1) * S_t * Fc + (sb0 + r) * Fc + my_i);  // + j R Fc floats
-      // ---- search: one sample per lane; the step word packs bin (bits 0-7), tie, open, dead (+ lane)
-      const int s_l = sb0 + lane;
+      const float* xs = L.sX + (T & 1) * Fc * xld + my_i * xld;
+      const int s_l = 32 * (my_w + Wf * jb) + lane;
       const bool v = live_w && s_l < ns;
       const float x = v ? xs[s_l] : 0.0f;
       int k = 0;
@@ -439,110 +506,157 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           k = min(hist_search(keys, x, a.lgk), n1);
         }
       }
+      // rank among the earlier samples of the same step (lanes 8 j .. 8 j + 7) in the same bin
+      const unsigned same = __match_any_sync(0xffffffffu, v ? (k | ((lane >> 3) << 16)) : (int)(0x40000000u | lane));
+      const int rank = __popc(same & lt);
       const float2 e = er[k];
-      const float t = quantize<QT>((x - e.x) * e.y);
       const bool tie = v && k > 0 && x == e.x;
       const bool open = ((openw[k >> 5] >> (k & 31)) & 1u) != 0u;
-      const int kk = v ? (k | (tie ? kTieBit : 0) | (open ? kOpenBit : 0)) : (kDeadBit | kOpenBit | (lane << 12));
-      const bool any_tie = __any_sync(0xffffffffu, tie);
-      // ---- phase 1: the steps' words, t, x and Q rows
-      int kv[J];
-      float tv[J], xv[J];
-      Row<VEC> Qr[J];
+      const int hf = k * (int)kRow | (tie ? kRecTie : 0) | (open || !v ? kRecOpen : 0) | (v ? 0 : kRecDead) |
+                     (rank << kRecRankShift);
+      const float t = v ? quantize<QT>((x - e.x) * e.y) : 0.0f;
+      sts_rec(rec_w + (uint32_t)lane * 16u, make_float4(__int_as_float(hf), t, x, e.y));
+      return __ballot_sync(0xffffffffu, rank >= 1);
+    };
+
+    // batch jb of tile T from the records: groups of JG steps, each phase by phase (records, tables and
+    // arithmetic; grad_x; last the ordered read-modify-writes of the sums), so that the independent work of
+    // the steps overlaps.  The gradient rows of a group are loaded one group ahead (g0: even groups, g1: odd).
+    auto run_batch = [&](GRaw<GT, VEC> (&g0)[JG], GRaw<GT, VEC> (&g1)[JG], int T, int jb, unsigned dup1) {
+      const int sb0 = 32 * (my_w + Wf * jb);
+      const uint32_t gxa = shared_addr(L.sGX + (T & 1) * S_t * Fc + (sb0 + r) * Fc + my_i);  // + j R Fc floats
+      // the steps go in groups of JG (registers: a group's records, units and sums are live together)
+      auto run_group = [&](const GRaw<GT, VEC> (&g)[JG], int h) {
+        // ---- phase 1: records, S / T units, q(g'), the epilogue sums and the grad_x shares
+        int hv[JG];
+        float tv[JG];
+        f2_t qv[JG][NP];
+        float gx[JG];
+        bool any_tie = false;
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int sj = j * R + r;
-        kv[j] = __shfl_sync(0xffffffffu, kk, sj);
-        tv[j] = __shfl_sync(0xffffffffu, t, sj);
-        xv[j] = LIN ? __shfl_sync(0xffffffffu, x, sj) : 0.0f;
-        lds_pairs<NP, WIDE>(Qr[j].p, qb + (uint32_t)(kv[j] & 0xff) * kRow);
-      }
-      // ---- phase 2: q(g'), the epilogue sums and the grad_x shares
-      f2_t qv[J][NP];
-      float gx[J];
+        for (int jj = 0; jj < JG; ++jj) {
+          const int j = h * JG + jj;
+          const float4 rec = lds_rec(rec_r + (uint32_t)(j * R * 16));
+          hv[jj] = __float_as_int(rec.x);
+          tv[jj] = rec.y;
+          const float xv = rec.z;
+          any_tie |= (hv[jj] & kRecTie) != 0;
+          const uint32_t sa = st_base + (uint32_t)(hv[jj] & ~kRecFlags);
+          f2_t S[NP], Tt[NP], gs[NP];
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        bool exact = false;
-        if constexpr (MASK != kMaskNone) exact = !__all_sync(0xffffffffu, (kv[j] & kOpenBit) != 0);
-        const uint32_t ho = (uint32_t)(kv[j] & 0xff) * (kRow / 2);
-        gx[j] = exact ? hist_body<QT, GT, VEC, MASK, EPIV, true>(g[j], tv[j], xv[j], Qr[j], sb + ho, tb + ho, pbias,
-                                                                 w0r, aw, ab, qv[j])
-                      : hist_body<QT, GT, VEC, MASK, EPIV, false>(g[j], tv[j], xv[j], Qr[j], 0u, 0u, pbias, w0r,
-                                                                  aw, ab, qv[j]);
-      }
-      // ---- phase 3: grad_x of the samples (edge sub-gradient where x == e_k, k > 0), the row's 4 lane
-      // shares summed by shuffles
-      if (do_gx) {
-        if (any_tie) {
+          for (int u = 0; u < NP; ++u) lds_unit(unit_addr<NP>(sa, u, d1), S[u], Tt[u]);
+          grad_pairs<GT, VEC>(g[jj], swap, gs);
+          bool exact = false;
+          if constexpr (MASK != kMaskNone) exact = !__all_sync(0xffffffffu, (hv[jj] & kRecOpen) != 0);
+          const f2_t t2 = pack2(tv[jj], tv[jj]);
+          f2_t d2 = 0ull, dw2 = 0ull;
+          const f2_t x2 = LIN ? pack2(xv, xv) : 0ull;
 #pragma unroll
-          for (int j = 0; j < J; ++j) {
-            const bool tj = (kv[j] & kTieBit) != 0;
-            if (__any_sync(0xffffffffu, tj)) {
-              const uint32_t kofs = (uint32_t)(kv[j] & 0xff) * kRow;
-              f2_t Qm[NP];
-              lds_pairs<NP, WIDE>(Qm, qb + (kofs != 0u ? kofs - kRow : 0u));
-              f2_t dp2 = 0ull;
+          for (int u = 0; u < NP; ++u) {
+            const f2_t g2 = gs[u];
+            if constexpr (LIN) {
+              dw2 = fma2(g2, w0r[u], dw2);
+              aw[u] = fma2(g2, x2, aw[u]);
+              ab[u] = add2(ab[u], g2);
+            }
+            f2_t qq = g2;
+            if constexpr (MASK != kMaskNone) {
+              if (exact) {
+                float p0, p1, g0, g1;
+                unpack2(fma2(t2, S[u], Tt[u]), p0, p1);
+                unpack2(g2, g0, g1);
+                if constexpr (MASK == kMaskReluBias) {
+                  round2<QT>(p0, p1);
+                  float b0, b1;
+                  unpack2(pbias[u], b0, b1);
+                  p0 += b0;
+                  p1 += b1;
+                  qq = pack2(p0 <= 0.f ? 0.f : g0, p1 <= 0.f ? 0.f : g1);
+                } else {
+                  qq = pack2(p0 <= thr ? 0.f : g0, p1 <= thr ? 0.f : g1);
+                }
+              }
+            }
+            if constexpr (EPIV == kEpvBias) aw[u] = add2(aw[u], qq);  // sum g' (before the QT rounding)
+            if constexpr (ROUND_G) {
+              float q0, q1;
+              unpack2(qq, q0, q1);
+              round2<QT>(q0, q1);
+              qq = pack2(q0, q1);
+            }
+            qv[jj][u] = qq;
+            d2 = fma2(qq, S[u], d2);
+          }
+          float lo, hi;
+          unpack2(d2, lo, hi);
+          float gxl = rec.w * (lo + hi);
+          if constexpr (LIN) {
+            unpack2(dw2, lo, hi);
+            gxl += lo + hi;
+          }
+          gx[jj] = gxl;
+        }
+        // ---- phase 2: grad_x (edge sub-gradient where x == e_k, k > 0), the row's 4 lane shares summed
+        if (do_gx) {
+          if (__any_sync(0xffffffffu, any_tie)) {
 #pragma unroll
-              for (int e2 = 0; e2 < NP; ++e2) dp2 = fma2(qv[j][e2], Qm[e2], dp2);
-              float lo, hi;
-              unpack2(dp2, lo, hi);
-              if (tj) gx[j] += lo + hi;
+            for (int jj = 0; jj < JG; ++jj) {
+          const int j = h * JG + jj;
+              const bool tj = (hv[jj] & kRecTie) != 0;
+              if (__any_sync(0xffffffffu, tj)) {
+                const int hk = hv[jj] & ~kRecFlags;
+                const int km = hk / (int)kRow;  // bin k of the sample
+                const uint32_t sa = st_base + (uint32_t)(hk != 0 ? hk - (int)kRow : 0);
+                f2_t dp2 = 0ull;
+#pragma unroll
+                for (int u = 0; u < NP; ++u) {
+                  f2_t Sm, Tm;
+                  lds_unit(unit_addr<NP>(sa, u, d1), Sm, Tm);
+                  dp2 = fma2(qv[jj][u], Sm, dp2);
+                }
+                float lo, hi;
+                unpack2(dp2, lo, hi);
+                if (tj) gx[jj] += er[km > 0 ? km - 1 : 0].y * (lo + hi);
+              }
             }
           }
+#pragma unroll
+          for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 1);
+#pragma unroll
+          for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 2);
+#pragma unroll
+          for (int jj = 0; jj < JG; ++jj)
+            if ((hv[jj] & kRecDead) == 0 && c == 0) sts_f32(gxa + (h * JG + jj) * R * Fc * 4, gx[jj]);
         }
+        // ---- phase 3: H += q(g'), U += q(t) q(g') into the warp's copy, step by step: the first samples of
+        // their bin, then (a step with a shared bin) the others, in rank order, out of line
 #pragma unroll
-        for (int j = 0; j < J; ++j) gx[j] += __shfl_xor_sync(0xffffffffu, gx[j], 1);
-#pragma unroll
-        for (int j = 0; j < J; ++j) gx[j] += __shfl_xor_sync(0xffffffffu, gx[j], 2);
-#pragma unroll
-        for (int j = 0; j < J; ++j)
-          if ((kv[j] & kDeadBit) == 0 && c == 0) sts_f32(gxa + j * R * Fc * 4, gx[j]);
-      }
-      // ---- phase 4: samples of a step that share a bin
-      unsigned dup[J];
-      bool any_dup = false;
-#pragma unroll
-      for (int j = 0; j < J; ++j) {
-        dup[j] = __match_any_sync(0xffffffffu, kv[j] & ~kTieBit) & cmask & lt;
-        any_dup |= dup[j] != 0u;
-      }
-      any_dup = __any_sync(0xffffffffu, any_dup);
-      // ---- phase 5: H += q(g'), U += q(t) q(g') into the warp's copy, step by step
-#pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const bool live = (kv[j] & kDeadBit) == 0;
-        const uint32_t kofs = (uint32_t)(kv[j] & 0xff) * kRow;
-        const float ta = par ? tv[j] : 1.0f, tb2 = par ? 1.0f : tv[j];
-        const f2_t wa = pack2(ta, ta), wb = pack2(tb2, tb2);
-        const uint32_t pa = aA + kofs, pb = aB + kofs;
-        auto rmw = [&]() {
-          f2_t A[NP], Bh[NP];
-          lds_pairs_ordered<NP, WIDE>(A, pa);
-          lds_pairs_ordered<NP, WIDE>(Bh, pb);
-#pragma unroll
-          for (int e2 = 0; e2 < NP; ++e2) {
-            A[e2] = fma2(wa, qv[j][e2], A[e2]);
-            Bh[e2] = fma2(wb, qv[j][e2], Bh[e2]);
-          }
-          sts_pairs_ordered<NP, WIDE>(pa, A);
-          sts_pairs_ordered<NP, WIDE>(pb, Bh);
-        };
-        if (!any_dup || !__any_sync(0xffffffffu, dup[j] != 0u)) {
-          if (live) rmw();
-        } else {
-          const int rank = __popc(dup[j]);
-          for (int rd = 0;; ++rd) {
-            if (live && rank == rd) rmw();
-            if (!__any_sync(0xffffffffu, rank > rd)) break;
-            __syncwarp();
+        for (int jj = 0; jj < JG; ++jj) {
+          const int j = h * JG + jj;
+          const int sel = hv[jj] & (kRecDead | kRecRank);
+          const uint32_t a0 = acc_base + (uint32_t)(hv[jj] & ~kRecFlags);
+          const f2_t t2 = pack2(tv[jj], tv[jj]);
+          hist_rmw<NP>(sel == 0 ? 1u : 0u, a0, d1, qv[jj], t2);
+          if ((dup1 >> (8 * j)) & 0xffu) {
+            const uint32_t live = (hv[jj] & kRecDead) ? 0u : 1u;
+            hist_rmw_rounds<NP>(live, (hv[jj] & kRecRank) >> kRecRankShift, a0, d1, qv[jj], t2);
           }
         }
+      };
+      // even groups run on g0 (the first loaded during the previous batch) while the next group loads into
+      // g1, odd groups on g1 while the group after them (the next batch's first after the last) loads into g0
+#pragma unroll
+      for (int h = 0; h < NG; h += 2) {
+        load_group(g1, h + 1);
+        run_group(g0, h);
+        load_group(g0, (h + 2) % NG);
+        run_group(g1, h + 1);
       }
     };
 
-    // tiles of S_t samples, JB (even) batches per warp per tile; gradient rows one batch ahead
-    GRaw<GT, VEC> gA[J], gB[J];
-    load_batch(gA);
+    // tiles of S_t samples, JB batches per warp per tile
+    GRaw<GT, VEC> g0[JG], g1[JG];
+    load_group(g0, 0);
 #pragma unroll 1
     for (int T = 0; T < n_tiles; ++T) {
       cp_async_wait_all();
@@ -553,41 +667,65 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         prefetch_g(T + 1);
       }
 #pragma unroll 1
-      for (int jb = 0; jb < JB; jb += 2) {
-        load_batch(gB);
-        run_batch(gA, T, jb);
-        load_batch(gA);
-        run_batch(gB, T, jb + 1);
+      for (int jb = 0; jb < JB; ++jb) {
+        const unsigned dup1 = search(T, jb);
+        __syncwarp();
+        run_batch(g0, g1, T, jb, dup1);
+        __syncwarp();  // every lane's reads of these records precede the next batch's search
       }
     }
     __syncthreads();  // every warp's sums and grad_x shares are in shared memory
     store_gx(n_tiles - 1);
 
-    // ---- epilogue sums: over the warp's 8 sample rows in row order, then the warps of a feature in order
+    // ---- epilogue sums: back to element order, over the warp's 8 sample rows in row order, then the
+    // warps of a feature in order
     if constexpr (ACC) {
-      Row<VEC> sw = aw, sb = ab;
+      if constexpr (NP == 2) {
+        const f2_t w0_ = aw[0], w1_ = aw[1], b0_ = ab[0], b1_ = ab[1];
+        aw[0] = swap ? w1_ : w0_;
+        aw[1] = swap ? w0_ : w1_;
+        ab[0] = swap ? b1_ : b0_;
+        ab[1] = swap ? b0_ : b1_;
+      }
+      f2_t sw[NP], sb[NP];
+#pragma unroll
+      for (int u = 0; u < NP; ++u) {
+        sw[u] = aw[u];
+        sb[u] = ab[u];
+      }
 #pragma unroll
       for (int r2 = 1; r2 < R; ++r2) {
 #pragma unroll
-        for (int e2 = 0; e2 < NP; ++e2) {
+        for (int u = 0; u < NP; ++u) {
           uint32_t lo, hi;
-          bits2(aw.p[e2], lo, hi);
-          const f2_t ow2 = from_bits2(__shfl_sync(0xffffffffu, lo, r2 * NC + c), __shfl_sync(0xffffffffu, hi, r2 * NC + c));
-          sw.p[e2] = add2(sw.p[e2], ow2);
+          bits2(aw[u], lo, hi);
+          sw[u] = add2(sw[u], from_bits2(__shfl_sync(0xffffffffu, lo, r2 * NC + c),
+                                         __shfl_sync(0xffffffffu, hi, r2 * NC + c)));
           if constexpr (LIN) {
-            bits2(ab.p[e2], lo, hi);
-            const f2_t ob2 = from_bits2(__shfl_sync(0xffffffffu, lo, r2 * NC + c), __shfl_sync(0xffffffffu, hi, r2 * NC + c));
-            sb.p[e2] = add2(sb.p[e2], ob2);
+            bits2(ab[u], lo, hi);
+            sb[u] = add2(sb[u], from_bits2(__shfl_sync(0xffffffffu, lo, r2 * NC + c),
+                                           __shfl_sync(0xffffffffu, hi, r2 * NC + c)));
           }
         }
       }
       if (live_w && r == 0) {
-        float* ep = L.sEpi + ((my_i * Wf + my_w) * 2) * D + cd;
-        sw.sts(ep);
-        if constexpr (LIN) sb.sts(ep + D);
+        float* ep = L.sEpi + ((my_i * Wf + my_w) * 2) * D + c * VEC;
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+          float lo, hi;
+          unpack2(sw[u], lo, hi);
+          ep[2 * u] = lo;
+          ep[2 * u + 1] = hi;
+          if constexpr (LIN) {
+            unpack2(sb[u], lo, hi);
+            ep[D + 2 * u] = lo;
+            ep[D + 2 * u + 1] = hi;
+          }
+        }
       }
     }
     // ---- the Wf copies of each feature summed in warp order into the first
+    const int BD2 = B * D * 2;
     for (int o = tid; o < fc * (BD2 / 4); o += nthr) {
       const int i = o / (BD2 / 4), off = o - i * (BD2 / 4);
       float4* base = reinterpret_cast<float4*>(L.sAcc + (size_t)i * Wf * BD2) + off;
@@ -607,8 +745,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int col = tid; col < fc * D; col += nthr) {
       const int i = col / D, d = col - i * D;
       const int n = L.sN[i];
-      const int cc = d / VEC, e = d - cc * VEC;
-      const float* h = L.sAcc + (size_t)i * Wf * BD2 + cc * CH + e;
+      const float* h = L.sAcc + (size_t)i * Wf * BD2 + unit_float<VEC>(d);
       float* row = ws + (int64_t)i * (B + 3) * D;
       if constexpr (ACC) {
         float s0 = 0.f, s1 = 0.f;
@@ -626,8 +763,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       float suffix = 0.f;
       for (int j = n - 1; j >= 0; --j) {
-        const float* hj = h + j * (NC * CH);
-        row[physical_bin(j, n, B) * D + d] = hj[VEC] + suffix;
+        const float* hj = h + j * (2 * D);
+        row[physical_bin(j, n, B) * D + d] = hj[2] + suffix;
         suffix += hj[0];
       }
       for (int p = n - 1; p < B - 1; ++p) row[p * D + d] = 0.f;  // padding rows
@@ -652,7 +789,7 @@ int launch_hist_t(BwdArgs a, cudaStream_t st) {
   auto kern = ple_bwd_hist_kernel<QT, GT, VEC, MASK, EPIV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
-  kern<<<grid, kBwdThreads, smem, st>>>(a, map);
+  kern<<<grid, kHistThreads, smem, st>>>(a, map);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error(e, "backward launch");
   return bwd_finalize(a, grid, st);

@@ -68,6 +68,7 @@ struct BwdArgs {
   int group, n_groups, g_wide;
   int g_prefetch;  // the gradient tensor map is valid (per-tile L2 prefetch)
   int gx_vec4;     // grad_x rows may be stored 16 bytes at a time (16-byte aligned, F % 4 == 0)
+  int hist_St;     // histogram kernel: samples per tile (a multiple of 32 x warps per feature)
 };
 
 struct EncArgs {
