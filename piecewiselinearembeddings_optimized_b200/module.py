@@ -152,8 +152,8 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
     Wraps an existing ``CudaPiecewiseLinearEmbeddings`` and the
     ``nn.Linear(F * D, H)`` that consumes its flattened output (parameters are
     shared, not copied), so it replaces ``nn.Sequential(embeddings,
-    nn.Flatten(), linear)`` in an MLP.  On CUDA under bf16 autocast the three
-    run as one tensor-core kernel (``rtdl_num_embeddings_cuda::
+    nn.Flatten(), linear)`` in an MLP.  With ``fused=True``, on CUDA under bf16
+    autocast the three run as one tensor-core kernel (``rtdl_num_embeddings_cuda::
     embeddings_linear_forward``) whose ``[N, F, D]`` intermediate never reaches
     memory; the result is bf16, as autocast's Linear returns.  With
     ``bf16_linear=True`` and no autocast the fp32 module output is rounded to
@@ -161,15 +161,16 @@ class CudaPiecewiseLinearEmbeddingsLinear(torch.nn.Module):
     fp16 autocast, plain fp32, d_embedding not a multiple of 8, more than 256
     bins) runs the composition: the module's own kernel followed by ``linear``.
 
-    ``fused=False`` always runs the composition.  The trade-off: the fused
-    kernel never allocates the ``[N, F, D]`` activation (805 MB at 65,536 rows
-    × 256 features × D = 24 in bf16), but on one B200 it is currently slower
-    than the composition at the measured shapes (e.g. 0.55 ms against 0.43 ms
-    for Linear(6144, 256) over 65,536 rows); see the repository's design notes.
+    The fused kernel is opt-in (``fused=True``); by default the module runs
+    the composition.  The trade-off: the fused kernel never allocates the
+    ``[N, F, D]`` activation (805 MB at 65,536 rows × 256 features × D = 24 in
+    bf16), but on one B200 it is slower than the composition at the measured
+    shapes (e.g. 0.55 ms against 0.43 ms for Linear(6144, 256) over 65,536
+    rows), so it pays only where that activation does not fit in memory.
     """
 
     def __init__(self, embeddings: CudaPiecewiseLinearEmbeddings, linear: torch.nn.Linear, *,
-                 bf16_linear: bool = False, fused: bool = True) -> None:
+                 bf16_linear: bool = False, fused: bool = False) -> None:
         super().__init__()
         d_in = embeddings.n_features * embeddings.d_embedding
         if linear.in_features != d_in:

@@ -194,7 +194,7 @@ def _modules(dev, version, d=16, h=96, seed=0):
     bins = [torch.from_numpy(b) for b in workloads.make_workload("c5", n=8, f=24, seed=seed).bins]
     emb = rc.CudaPiecewiseLinearEmbeddings([b.to(dev) for b in bins], d, activation=True, version=version).to(dev)
     lin = torch.nn.Linear(len(bins) * d, h).to(dev)
-    return emb, lin, rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin)
+    return emb, lin, rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin, fused=True)
 
 
 @pytest.mark.gpu
@@ -256,9 +256,23 @@ def test_module_more_than_256_bins_runs_the_composition(cuda_device):
     emb = rc.CudaPiecewiseLinearEmbeddings([b.to(cuda_device) for b in bins], 16, activation=True,
                                            version="A").to(cuda_device)
     lin = torch.nn.Linear(len(bins) * 16, 32).to(cuda_device)
-    fused = rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin)
+    fused = rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin, fused=True)
     x = torch.randn(64, len(bins), device=cuda_device) * 40
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         z = fused(x)
         assert z.dtype == torch.bfloat16
         assert torch.equal(z, lin(emb(x).flatten(1)))
+
+
+@pytest.mark.gpu
+def test_module_default_runs_the_composition(cuda_device):
+    """Without fused=True the wrapper is exactly the composition (the fused kernel is opt-in: slower on the
+    measured shapes), under autocast too."""
+    import rtdl_num_embeddings_cuda as rc
+
+    emb, lin, _ = _modules(cuda_device, "B")
+    plain = rc.CudaPiecewiseLinearEmbeddingsLinear(emb, lin)
+    assert plain.fused is False
+    x = torch.randn(77, emb.n_features, device=cuda_device)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        assert torch.equal(plain(x), lin(emb(x).flatten(1)))
