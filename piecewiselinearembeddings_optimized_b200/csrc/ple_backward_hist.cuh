@@ -251,57 +251,35 @@ __device__ __forceinline__ uint32_t unit_addr(uint32_t a0, int u, uint32_t d1) {
   else return a0 + 16u * u;
 }
 
-// H += g', U += t g' for the lane's NP units of one sample, when `live` (predicated, no branch).
+// H += g', U += t g' for the lane's NP units of one sample, when `live` (predicated loads and stores; the
+// arithmetic in between runs on every lane).
 template <int NP>
 __device__ __forceinline__ void hist_rmw(uint32_t live, uint32_t a0, uint32_t d1, const f2_t (&g)[NP], f2_t t2) {
-  if constexpr (NP == 1) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0;\n\t"
-        "setp.ne.u32 p, %0, 0;\n\t"
-        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
-        "@p add.rn.f32x2 h0, h0, %2;\n\t"
-        "@p fma.rn.f32x2 u0, %3, %2, u0;\n\t"
-        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t}" ::"r"(live),
-        "r"(a0), "l"(g[0]), "l"(t2)
-        : "memory");
-  } else if constexpr (NP == 2) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0, h1, u1;\n\t"
-        "setp.ne.u32 p, %0, 0;\n\t"
-        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
-        "@p ld.shared.v2.b64 {h1, u1}, [%2];\n\t"
-        "@p add.rn.f32x2 h0, h0, %3;\n\t"
-        "@p fma.rn.f32x2 u0, %5, %3, u0;\n\t"
-        "@p add.rn.f32x2 h1, h1, %4;\n\t"
-        "@p fma.rn.f32x2 u1, %5, %4, u1;\n\t"
-        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t"
-        "@p st.shared.v2.b64 [%2], {h1, u1};\n\t}" ::"r"(live),
-        "r"(a0), "r"(unit_addr<2>(a0, 1, d1)), "l"(g[0]), "l"(g[1]), "l"(t2)
-        : "memory");
-  } else {
-    static_assert(NP == 3, "pair units per lane: 1, 2 or 3");
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t.reg .b64 h0, u0, h1, u1, h2, u2;\n\t"
-        "setp.ne.u32 p, %0, 0;\n\t"
-        "@p ld.shared.v2.b64 {h0, u0}, [%1];\n\t"
-        "@p ld.shared.v2.b64 {h1, u1}, [%1+16];\n\t"
-        "@p ld.shared.v2.b64 {h2, u2}, [%1+32];\n\t"
-        "@p add.rn.f32x2 h0, h0, %2;\n\t"
-        "@p fma.rn.f32x2 u0, %5, %2, u0;\n\t"
-        "@p add.rn.f32x2 h1, h1, %3;\n\t"
-        "@p fma.rn.f32x2 u1, %5, %3, u1;\n\t"
-        "@p add.rn.f32x2 h2, h2, %4;\n\t"
-        "@p fma.rn.f32x2 u2, %5, %4, u2;\n\t"
-        "@p st.shared.v2.b64 [%1], {h0, u0};\n\t"
-        "@p st.shared.v2.b64 [%1+16], {h1, u1};\n\t"
-        "@p st.shared.v2.b64 [%1+32], {h2, u2};\n\t}" ::"r"(live),
-        "r"(a0), "l"(g[0]), "l"(g[1]), "l"(g[2]), "l"(t2)
-        : "memory");
+  f2_t h[NP], u[NP];
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    const uint32_t ad = e == 0 ? a0 : (NP == 2 ? a0 + d1 : a0 + 16u * e);
+    // lanes that do not take part read zeros (their arithmetic is discarded by the store's predicate); the
+    // registers are written on every lane, which keeps a predicated-off load from extending their live range
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\tmov.b64 %0, 0;\n\tmov.b64 %1, 0;\n\t"
+                 "@p ld.shared.v2.b64 {%0, %1}, [%3];\n\t}"
+                 : "=l"(h[e]), "=l"(u[e]) : "r"(live), "r"(ad) : "memory");
+  }
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    h[e] = add2(h[e], g[e]);
+    u[e] = fma2(t2, g[e], u[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    const uint32_t ad = e == 0 ? a0 : (NP == 2 ? a0 + d1 : a0 + 16u * e);
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %0, 0;\n\t@p st.shared.v2.b64 [%1], {%2, %3};\n\t}"
+                 ::"r"(live), "r"(ad), "l"(h[e]), "l"(u[e]) : "memory");
   }
 }
 
-// Rounds 1, 2, ... of the ordered read-modify-writes of one step whose samples share a bin (kept out of
-// line: inlined, the rounds raised the register pressure of the whole loop into spills).
+// Rounds 2, 3, ... of the ordered read-modify-writes of one step (a bin shared by three or more of its
+// samples; rare, so kept out of line).
 template <int NP>
 __device__ __noinline__ void hist_rmw_rounds(uint32_t live, int rank, uint32_t a0, uint32_t d1, f2_t q0, f2_t q1,
                                              f2_t q2, f2_t t2) {
@@ -309,7 +287,7 @@ __device__ __noinline__ void hist_rmw_rounds(uint32_t live, int rank, uint32_t a
   q[0] = q0;
   if constexpr (NP > 1) q[1] = q1;
   if constexpr (NP > 2) q[2] = q2;
-  for (int rd = 1;; ++rd) {
+  for (int rd = 2;; ++rd) {
     __syncwarp();
     hist_rmw<NP>(live && rank == rd ? 1u : 0u, a0, d1, q, t2);
     if (!__any_sync(0xffffffffu, rank > rd)) break;
@@ -340,7 +318,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
     ple_bwd_hist_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap gmap) {
   constexpr int NC = kHistNC, R = 32 / NC, J = NC;  // lanes per row, samples per step, steps per batch
   // steps processed together (registers: a group's records, units and sums are live together)
-  constexpr int JG = VEC == 6 ? 1 : 2;
+  constexpr int JG = 2;
   constexpr int NG = J / JG;  // groups per batch (even)
   constexpr int D = NC * VEC;
   constexpr int NP = VEC / 2;
@@ -486,8 +464,8 @@ __global__ void __launch_bounds__(kHistThreads, 1)
 
     // search of batch jb of tile T (samples 32 (my_w + Wf jb) + lane of the tile), one sample per lane: its
     // record {bin row offset | flags, q(t), x, r_k}; returns the ballot (bit j 8 + r) of the samples with rank
-    // >= 1 among the samples of their step in their bin
-    auto search = [&](int T, int jb) -> unsigned {
+    // >= 1 among the samples of their step in their bin, and in dup2 that of rank >= 2
+    auto search = [&](int T, int jb, unsigned& dup2) -> unsigned {
       const int64_t t0 = s_begin + (int64_t)T * S_t;
       const int ns = (int)min64(S_t, s_end - t0);
       const float* xs = L.sX + (T & 1) * Fc * xld + my_i * xld;
@@ -516,13 +494,15 @@ __global__ void __launch_bounds__(kHistThreads, 1)
                      (rank << kRecRankShift);
       const float t = v ? quantize<QT>((x - e.x) * e.y) : 0.0f;
       sts_rec(rec_w + (uint32_t)lane * 16u, make_float4(__int_as_float(hf), t, x, e.y));
+      dup2 = __ballot_sync(0xffffffffu, rank >= 2);
       return __ballot_sync(0xffffffffu, rank >= 1);
     };
 
     // batch jb of tile T from the records: groups of JG steps, each phase by phase (records, tables and
     // arithmetic; grad_x; last the ordered read-modify-writes of the sums), so that the independent work of
     // the steps overlaps.  The gradient rows of a group are loaded one group ahead (g0: even groups, g1: odd).
-    auto run_batch = [&](GRaw<GT, VEC> (&g0)[JG], GRaw<GT, VEC> (&g1)[JG], int T, int jb, unsigned dup1) {
+    auto run_batch = [&](GRaw<GT, VEC> (&g0)[JG], GRaw<GT, VEC> (&g1)[JG], int T, int jb, unsigned dup1,
+                         unsigned dup2) {
       const int sb0 = 32 * (my_w + Wf * jb);
       const uint32_t gxa = shared_addr(L.sGX + (T & 1) * S_t * Fc + (sb0 + r) * Fc + my_i);  // + j R Fc floats
       // the steps go in groups of JG (registers: a group's records, units and sums are live together)
@@ -629,7 +609,8 @@ __global__ void __launch_bounds__(kHistThreads, 1)
             if ((hv[jj] & kRecDead) == 0 && c == 0) sts_f32(gxa + (h * JG + jj) * R * Fc * 4, gx[jj]);
         }
         // ---- phase 3: H += q(g'), U += q(t) q(g') into the warp's copy, step by step: the first samples of
-        // their bin, then (a step with a shared bin) the others, in rank order, out of line
+        // their bin, then, in a step with a shared bin, the second ones, then, rarely (a bin shared by three
+        // or more samples of the step), the rest out of line
 #pragma unroll
         for (int jj = 0; jj < JG; ++jj) {
           const int j = h * JG + jj;
@@ -637,9 +618,13 @@ __global__ void __launch_bounds__(kHistThreads, 1)
           const uint32_t a0 = acc_base + (uint32_t)(hv[jj] & ~kRecFlags);
           const f2_t t2 = pack2(tv[jj], tv[jj]);
           hist_rmw<NP>(sel == 0 ? 1u : 0u, a0, d1, qv[jj], t2);
-          if ((dup1 >> (8 * j)) & 0xffu) {
-            const uint32_t live = (hv[jj] & kRecDead) ? 0u : 1u;
-            hist_rmw_rounds<NP>(live, (hv[jj] & kRecRank) >> kRecRankShift, a0, d1, qv[jj], t2);
+          if ((dup1 >> (8 * j)) & 0xffu) {  // uniform: the step has a shared bin
+            __syncwarp();
+            hist_rmw<NP>(sel == (1 << kRecRankShift) ? 1u : 0u, a0, d1, qv[jj], t2);
+            if ((dup2 >> (8 * j)) & 0xffu) {
+              const uint32_t live = (hv[jj] & kRecDead) ? 0u : 1u;
+              hist_rmw_rounds<NP>(live, (hv[jj] & kRecRank) >> kRecRankShift, a0, d1, qv[jj], t2);
+            }
           }
         }
       };
@@ -668,9 +653,10 @@ __global__ void __launch_bounds__(kHistThreads, 1)
       }
 #pragma unroll 1
       for (int jb = 0; jb < JB; ++jb) {
-        const unsigned dup1 = search(T, jb);
+        unsigned dup2;
+        const unsigned dup1 = search(T, jb, dup2);
         __syncwarp();
-        run_batch(g0, g1, T, jb, dup1);
+        run_batch(g0, g1, T, jb, dup1, dup2);
         __syncwarp();  // every lane's reads of these records precede the next batch's search
       }
     }
