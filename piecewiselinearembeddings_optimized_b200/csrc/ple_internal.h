@@ -17,6 +17,7 @@ constexpr int kBwdThreads = 512;
 // forward tuning
 constexpr int kFwdMaxThreads = 512;
 constexpr size_t kFwdTableBudget = 64 * 1024;
+constexpr size_t kFwdTableBudgetF32 = 128 * 1024;  // fp32 outputs with D <= 16 (see launch_forward)
 constexpr int kFwdPairsPerTile = 2048;  // measured: 2048 beats 512 and 1024 on the c4 and c5 forwards
 
 struct FwdArgs {
