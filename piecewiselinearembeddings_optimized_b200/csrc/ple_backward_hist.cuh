@@ -13,8 +13,9 @@
 // workspace blocks are those of the sorted kernel (the finalize is shared).
 // A chunk's warps split evenly over its features (Wf = 16 / Fc per feature)
 // and each warp owns a private copy of its feature's H / U sums, so no two
-// warps ever write the same word.  A D row is 4 lanes x VEC elements; a warp
-// step is 8 samples (rows).  Per tile of S_t samples (x arrives by cp.async
+// warps ever write the same word.  A D row is 4 lanes x VEC elements (D = 8,
+// 16: a warp step is 8 samples) or, for D = 24, 8 lane slots of which 6 hold
+// 4 elements each (a warp step is 4 samples).  Per tile of S_t samples (x arrives by cp.async
 // one tile ahead, the next tile's gradient rows are prefetched into L2 by one
 // tensor-map instruction per 256 rows) each warp takes batches of 32 samples
 // of its feature, interleaved with the feature's other warps:
@@ -22,12 +23,12 @@
 //     an L-level descent over the interior edges in breadth-first order); the
 //     sample's record {bin row offset | flags, q(t), x, r_k} goes to the
 //     warp's record buffer;
-//   * 4 steps of 8 samples: each lane reads its row's record (one 16-byte
-//     load, shared by the row's 4 lanes), the S / T units of the sample's bin,
+//   * 4 steps of 8 samples (8 of 4 at D = 24): each lane reads its row's record
+//     (one 16-byte load, shared by the row's lanes), the S / T units of the sample's bin,
 //     computes q(g') (the ReLU mask; skipped, bit-identically, when every
 //     sample of the step is in an "open" bin, one whose ReLU input is positive
 //     for every t it admits), the epilogue sums, its share of grad_x (summed
-//     over the row's 4 lanes by shuffles);
+//     over the row's lanes by shuffles);
 //   * then, step by step, H += q(g'), U += q(t) q(g') into the warp's copy
 //     (one predicated 16-byte read-modify-write per element pair).  Samples of
 //     one step that share a bin (found by match.any) update it in rounds, in
@@ -38,7 +39,10 @@
 // c NP .. c NP + NP - 1 (NP = VEC / 2).  With NP = 2 (D = 16) a bin row is 128
 // bytes and the lanes of odd rows take their two units in the opposite order
 // (their gradient pairs swapped to match), so the two rows that share a
-// 128-byte wavefront read disjoint bank groups whatever their bins.
+// 128-byte wavefront read disjoint bank groups whatever their bins.  With D = 24
+// a bin row is 256 bytes laid out unit-major (unit u of lane c at u 8 + c), so
+// a 128-byte wavefront serves one row and has no conflict at all (a 192-byte
+// lane-major row conflicts whenever two rows' bins have the same parity).
 // At the end of a segment the Wf copies of a feature are summed in warp order,
 // a suffix scan over bins turns H / U into grad_W and the partial goes to the
 // workspace.  No floating-point atomics: bitwise deterministic for a given
@@ -49,7 +53,14 @@
 
 namespace ple {
 
-constexpr int kHistNC = 4;  // lanes per D row: 8 samples per warp step, 4 steps per batch of 32
+constexpr int kHistNC = 4;  // lanes per D row (d_embedding 8 / 16): 8 samples per warp step, 4 steps per batch of 32
+
+// Lane slots per sample row: 4 for d_embedding 8 and 16 (VEC = D / 4 elements each); 8 for d_embedding 24
+// (6 active lanes of 4 elements, 2 idle), whose bin rows are laid out unit-major so that one 128-byte
+// wavefront serves one row and never meets a bank conflict.
+__host__ __device__ constexpr int hist_lanes(int D) { return D == 24 ? 8 : kHistNC; }
+// Bytes of one bin row of pair units (S / T table, H / U sums).
+__host__ __device__ constexpr int hist_row_bytes(int D) { return D == 24 ? 256 : 8 * D; }
 // 16 warps per CTA (128 registers a thread; measured faster than 12 warps with 168 registers)
 constexpr int kHistWarps = 16, kHistThreads = 32 * kHistWarps;
 
@@ -59,8 +70,8 @@ constexpr int kRecTie = 1, kRecOpen = 2, kRecDead = 4, kRecRankShift = 3, kRecRa
 constexpr int kRecFlags = 63;
 
 struct HistLayout {
-  float* sAcc;      // [16 warps][B][2 D] private H / U units
-  float* sST;       // [Fc][B][2 D] S / T units, logical bin order
+  float* sAcc;      // [16 warps][B][row] private H / U units
+  float* sST;       // [Fc][B][row] S / T units, logical bin order
   float* sX;        // [2][Fc][S_t + 8] x tiles (transposed; the pad spreads the cp.async stores over banks)
   float* sGX;       // [2][S_t][Fc] grad_x tiles
   float4* sRec;     // [16 warps][32] sample records of the current batch
@@ -83,8 +94,8 @@ __host__ __device__ __forceinline__ size_t hist_layout_bytes(int B, int D, int F
     off += (bytes + 127) & ~(size_t)127;  // 128-byte aligned: bin rows start on a bank-window boundary
     return base + o;
   };
-  unsigned char* pAcc = take((size_t)kHistWarps * B * D * 2 * 4);
-  unsigned char* pST = take((size_t)Fc * B * D * 2 * 4);
+  unsigned char* pAcc = take((size_t)kHistWarps * B * hist_row_bytes(D));
+  unsigned char* pST = take((size_t)Fc * B * hist_row_bytes(D));
   unsigned char* pX = take((size_t)2 * Fc * hist_xld(S_t) * 4);
   unsigned char* pGX = take((size_t)2 * S_t * Fc * 4);
   unsigned char* pRec = take((size_t)kHistWarps * 32 * 16);
@@ -108,20 +119,22 @@ __host__ __device__ __forceinline__ size_t hist_layout_bytes(int B, int D, int F
   return off;
 }
 
-// Float offset of element d inside a bin row of 16-byte pair units (S or H at +0, T or U at +2).
-template <int VEC>
+// Float offset of element d inside a bin row of 16-byte pair units (S or H at +0, T or U at +2): lane-major
+// with 4 lanes a row (lane c's units at c NP + u), unit-major with 8 (unit u of lane c at u 8 + c).
+template <int VEC, int NCL>
 __device__ __forceinline__ int unit_float(int d) {
   constexpr int NP = VEC / 2;
   const int c = d / VEC, e = d - c * VEC;
-  return (c * NP + (e >> 1)) * 4 + (e & 1);
+  if constexpr (NCL == 8) return ((e >> 1) * NCL + c) * 4 + (e & 1);
+  else return (c * NP + (e >> 1)) * 4 + (e & 1);
 }
 
 // The chunk's tables for one segment and zeroed private sums: search keys, {e_k, r_k}, S = q(W) and its
 // exclusive prefix T in logical bin order (pair units), the open bits.
-template <typename QT, int MASK, int VEC>
+template <typename QT, int MASK, int VEC, int NCL>
 __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLayout& L, int f0, int fc, int Fc,
                                                   int nkeys, int lgk, int tid, int nthr) {
-  const int B = a.B, D = a.D, D2 = 2 * D;
+  const int B = a.B, D = a.D, D2 = hist_row_bytes(D) / 4;  // floats of a bin row
   const int ow = (B + 31) / 32;
   for (int i = tid; i < Fc; i += nthr) {
     const int n = i < fc ? a.n_bins[f0 + i] : 1;
@@ -161,13 +174,13 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
     const int i = row / B, p = row - i * B;
     const int n = L.sN[i];
     const int lg = (p == B - 1) ? n - 1 : (p < n - 1 ? p : -1);
-    if (lg >= 0) L.sST[(i * B + lg) * D2 + unit_float<VEC>(d)] = quantize<QT>(Wc[idx]);
+    if (lg >= 0) L.sST[(i * B + lg) * D2 + unit_float<VEC, NCL>(d)] = quantize<QT>(Wc[idx]);
   }
   __syncthreads();
   for (int col = tid; col < Fc * D; col += nthr) {
     const int i = col / D, d = col - i * D;
     const int n = L.sN[i];
-    const int uo = unit_float<VEC>(d);
+    const int uo = unit_float<VEC, NCL>(d);
     float acc = 0.0f;
     for (int j = 0; j < n; ++j) {
       float* u = L.sST + (i * B + j) * D2 + uo;
@@ -190,7 +203,7 @@ __device__ __forceinline__ void stage_hist_tables(const BwdArgs& a, const HistLa
         const float tmax = last ? 0.0f : quantize<QT>((a.edges[(int64_t)(f0 + i) * (B + 1) + k + 1] - er.x) * er.y);
         open = true;
         for (int d = 0; d < D && open; ++d) {
-          const float* u = L.sST + (i * B + k) * D2 + unit_float<VEC>(d);
+          const float* u = L.sST + (i * B + k) * D2 + unit_float<VEC, NCL>(d);
           const float S = u[0], T = u[2];
           const float bias = MASK == kMaskReluBias ? a.bias[(int64_t)(f0 + i) * D + d] : 0.0f;
           const float p0 = fmaf(0.0f, S, T), p1 = fmaf(tmax, S, T);
@@ -313,19 +326,22 @@ __device__ __forceinline__ void grad_pairs(const GRaw<GT, VEC>& g, bool swap, f2
   }
 }
 
-template <typename QT, typename GT, int VEC, int MASK, int EPIV>
+template <typename QT, typename GT, int VEC, int MASK, int EPIV, int NCL>
 __global__ void __launch_bounds__(kHistThreads, 1)
     ple_bwd_hist_kernel(const BwdArgs a, const __grid_constant__ CUtensorMap gmap) {
-  constexpr int NC = kHistNC, R = 32 / NC, J = NC;  // lanes per row, samples per step, steps per batch
+  constexpr int NC = NCL, R = 32 / NC, J = NC;  // lane slots per row, samples per step, steps per batch
   // steps processed together (registers: a group's records, units and sums are live together)
   constexpr int JG = 2;
   constexpr int NG = J / JG;  // groups per batch (even)
-  constexpr int D = NC * VEC;
+  constexpr int D = NC == 8 ? 24 : NC * VEC;
+  constexpr int NA = D / VEC;  // active lanes of a row
+  static_assert(NC == 4 || (NC == 8 && VEC == 4), "8 lane slots only for d_embedding 24");
   constexpr int NP = VEC / 2;
   constexpr bool LIN = EPIV == kEpvLin;
   constexpr bool ACC = EPIV != kEpvNone;
   constexpr bool ROUND_G = !std::is_same<GT, QT>::value && !std::is_same<QT, float>::value;
-  constexpr uint32_t kRow = 2 * D * 4;  // bytes of a bin row (S / T units, H / U units)
+  constexpr uint32_t kRow = hist_row_bytes(D);  // bytes of a bin row (S / T units, H / U units)
+  static_assert(kRow == (uint32_t)NP * NC * 16, "pair units of a row");
   static_assert(VEC == 2 || VEC == 4 || VEC == 6, "the histogram kernel packs 1 to 3 fp32 pairs per lane");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int B = a.B;
@@ -340,9 +356,9 @@ __global__ void __launch_bounds__(kHistThreads, 1)
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int lane = tid & 31, wid = tid >> 5;
   const int r = lane / NC, c = lane - r * NC;
-  const bool swap = NP == 2 && (r & 1) != 0;
+  const bool active = c < NA;  // idle lanes (8 slots at D = 24) load nothing and add zeros to the row's pad
+  const bool swap = NP == 2 && NC == 4 && (r & 1) != 0;
   const int my_i = wid / Wf, my_w = wid - my_i * Wf;
-  const unsigned cmask = 0x11111111u << c;  // lanes holding chunk c of their row (NC == 4)
   const unsigned lt = (1u << lane) - 1u;
   const int JB = S_t / (32 * Wf);  // batches per warp per tile (even: the host plans it so)
   const bool do_gx = a.grad_x != nullptr;
@@ -350,8 +366,10 @@ __global__ void __launch_bounds__(kHistThreads, 1)
   const uint64_t pol_first = l2_policy_evict_first();
   const float thr = zero_round_threshold<QT>();
   // this lane's first unit inside a bin row (odd rows of D = 16 start with the second pair)
-  const uint32_t lane_unit = (uint32_t)(c * NP + (swap ? 1 : 0)) * 16u;
-  const uint32_t d1 = swap ? (uint32_t)-16 : 16u;  // from the lane's first unit to its second (NP == 2)
+  // this lane's first unit inside a bin row and the step to its second (NP == 2): lane-major rows (odd rows
+  // of D = 16 start with the second pair) or unit-major rows (D = 24)
+  const uint32_t lane_unit = NC == 8 ? (uint32_t)c * 16u : (uint32_t)(c * NP + (swap ? 1 : 0)) * 16u;
+  const uint32_t d1 = NC == 8 ? (uint32_t)NC * 16u : swap ? (uint32_t)-16 : 16u;
   const uint32_t acc_base = shared_addr(L.sAcc) + (uint32_t)wid * B * kRow + lane_unit;
   const uint32_t rec_w = shared_addr(L.sRec + wid * 32);
   const uint32_t rec_r = rec_w + (uint32_t)r * 16u;
@@ -413,7 +431,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
     __syncthreads();  // previous segment finished with every shared buffer
     load_x(0);
     prefetch_g(0);
-    stage_hist_tables<QT, MASK, VEC>(a, L, f0, fc, Fc, nkeys, a.lgk, tid, nthr);
+    stage_hist_tables<QT, MASK, VEC, NCL>(a, L, f0, fc, Fc, nkeys, a.lgk, tid, nthr);
 
     // per-lane epilogue parameters and sums, in this lane's unit order
     f2_t pbias[NP], w0r[NP], aw[NP], ab[NP];  // aw: sum g x (B) or sum g' (A); ab: sum g (B)
@@ -425,10 +443,10 @@ __global__ void __launch_bounds__(kHistThreads, 1)
       ab[u] = 0ull;
       const int e0 = c * VEC + 2 * ((NP == 2 && swap) ? 1 - u : u);
       if constexpr (MASK == kMaskReluBias) {
-        if (live_w) pbias[u] = pack2(a.bias[(int64_t)(f0 + my_i) * D + e0], a.bias[(int64_t)(f0 + my_i) * D + e0 + 1]);
+        if (live_w && active) pbias[u] = pack2(a.bias[(int64_t)(f0 + my_i) * D + e0], a.bias[(int64_t)(f0 + my_i) * D + e0 + 1]);
       }
       if constexpr (LIN) {
-        if (live_w) w0r[u] = pack2(a.w0[(int64_t)(f0 + my_i) * D + e0], a.w0[(int64_t)(f0 + my_i) * D + e0 + 1]);
+        if (live_w && active) w0r[u] = pack2(a.w0[(int64_t)(f0 + my_i) * D + e0], a.w0[(int64_t)(f0 + my_i) * D + e0 + 1]);
       }
     }
     const float* keys = L.sKey + my_i * nkeys;
@@ -449,7 +467,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
 #pragma unroll
       for (int jj = 0; jj < JG; ++jj) {
         const int j = h * JG + jj;
-        if (live_w && j * R < srem) {
+        if (live_w && active && j * R < srem) {
           ldg_raw<GT, VEC>(g[jj], gp + j * gstep, wide, pol_first);
         } else {
 #pragma unroll
@@ -485,7 +503,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
         }
       }
       // rank among the earlier samples of the same step (lanes 8 j .. 8 j + 7) in the same bin
-      const unsigned same = __match_any_sync(0xffffffffu, v ? (k | ((lane >> 3) << 16)) : (int)(0x40000000u | lane));
+      const unsigned same = __match_any_sync(0xffffffffu, v ? (k | ((lane / R) << 16)) : (int)(0x40000000u | lane));
       const int rank = __popc(same & lt);
       const float2 e = er[k];
       const bool tie = v && k > 0 && x == e.x;
@@ -604,6 +622,10 @@ __global__ void __launch_bounds__(kHistThreads, 1)
           for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 1);
 #pragma unroll
           for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 2);
+          if constexpr (NC == 8) {
+#pragma unroll
+            for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 4);
+          }
 #pragma unroll
           for (int jj = 0; jj < JG; ++jj)
             if ((hv[jj] & kRecDead) == 0 && c == 0) sts_f32(gxa + (h * JG + jj) * R * Fc * 4, gx[jj]);
@@ -618,10 +640,10 @@ __global__ void __launch_bounds__(kHistThreads, 1)
           const uint32_t a0 = acc_base + (uint32_t)(hv[jj] & ~kRecFlags);
           const f2_t t2 = pack2(tv[jj], tv[jj]);
           hist_rmw<NP>(sel == 0 ? 1u : 0u, a0, d1, qv[jj], t2);
-          if ((dup1 >> (8 * j)) & 0xffu) {  // uniform: the step has a shared bin
+          if ((dup1 >> (R * j)) & ((1u << R) - 1u)) {  // uniform: the step has a shared bin
             __syncwarp();
             hist_rmw<NP>(sel == (1 << kRecRankShift) ? 1u : 0u, a0, d1, qv[jj], t2);
-            if ((dup2 >> (8 * j)) & 0xffu) {
+            if ((dup2 >> (R * j)) & ((1u << R) - 1u)) {
               const uint32_t live = (hv[jj] & kRecDead) ? 0u : 1u;
               hist_rmw_rounds<NP>(live, (hv[jj] & kRecRank) >> kRecRankShift, a0, d1, qv[jj], t2);
             }
@@ -694,7 +716,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
           }
         }
       }
-      if (live_w && r == 0) {
+      if (live_w && r == 0 && active) {
         float* ep = L.sEpi + ((my_i * Wf + my_w) * 2) * D + c * VEC;
 #pragma unroll
         for (int u = 0; u < NP; ++u) {
@@ -711,7 +733,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
       }
     }
     // ---- the Wf copies of each feature summed in warp order into the first
-    const int BD2 = B * D * 2;
+    const int BD2 = B * (int)(kRow / 4);  // floats of one warp's copy
     for (int o = tid; o < fc * (BD2 / 4); o += nthr) {
       const int i = o / (BD2 / 4), off = o - i * (BD2 / 4);
       float4* base = reinterpret_cast<float4*>(L.sAcc + (size_t)i * Wf * BD2) + off;
@@ -731,7 +753,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
     for (int col = tid; col < fc * D; col += nthr) {
       const int i = col / D, d = col - i * D;
       const int n = L.sN[i];
-      const float* h = L.sAcc + (size_t)i * Wf * BD2 + unit_float<VEC>(d);
+      const float* h = L.sAcc + (size_t)i * Wf * BD2 + unit_float<VEC, NCL>(d);
       float* row = ws + (int64_t)i * (B + 3) * D;
       if constexpr (ACC) {
         float s0 = 0.f, s1 = 0.f;
@@ -749,7 +771,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
       }
       float suffix = 0.f;
       for (int j = n - 1; j >= 0; --j) {
-        const float* hj = h + j * (2 * D);
+        const float* hj = h + j * (int)(kRow / 4);
         row[physical_bin(j, n, B) * D + d] = hj[2] + suffix;
         suffix += hj[0];
       }
@@ -762,7 +784,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
 // Host: plan (ple_backward.cu) and launch.
 int hist_prepare(BwdArgs& a, size_t* smem, int* grid);
 
-template <typename QT, typename GT, int VEC, int MASK, int EPIV>
+template <typename QT, typename GT, int VEC, int MASK, int EPIV, int NCL>
 int launch_hist_t(BwdArgs a, cudaStream_t st) {
   size_t smem = 0;
   int grid = 0;
@@ -772,7 +794,7 @@ int launch_hist_t(BwdArgs a, cudaStream_t st) {
   CUtensorMap map;
   a.g_prefetch = bwd_grad_map(a, std::is_same<GT, float>::value ? 0 : std::is_same<GT, __nv_bfloat16>::value ? 2 : 1,
                               &map) ? 1 : 0;
-  auto kern = ple_bwd_hist_kernel<QT, GT, VEC, MASK, EPIV>;
+  auto kern = ple_bwd_hist_kernel<QT, GT, VEC, MASK, EPIV, NCL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_cuda_error(e, "cudaFuncSetAttribute(backward)");
   kern<<<grid, kHistThreads, smem, st>>>(a, map);
@@ -782,17 +804,19 @@ int launch_hist_t(BwdArgs a, cudaStream_t st) {
 }
 
 // Mask variant and epilogue terms (as launch_bwd_mask of the sorted kernel).
-template <typename QT, typename GT, int VEC>
+template <typename QT, typename GT, int VEC, int NCL>
 int launch_hist_mask(const BwdArgs& a, cudaStream_t st) {
   const bool lin = a.epi == kEpiB && (a.grad_x || a.grad_w0 || a.grad_b0);
   const bool bias = a.epi == kEpiA && a.grad_bias;
   if (a.relu && a.epi == kEpiA)
-    return bias ? launch_hist_t<QT, GT, VEC, kMaskReluBias, kEpvBias>(a, st)
-                : launch_hist_t<QT, GT, VEC, kMaskReluBias, kEpvNone>(a, st);
+    return bias ? launch_hist_t<QT, GT, VEC, kMaskReluBias, kEpvBias, NCL>(a, st)
+                : launch_hist_t<QT, GT, VEC, kMaskReluBias, kEpvNone, NCL>(a, st);
   if (a.relu)
-    return lin ? launch_hist_t<QT, GT, VEC, kMaskRelu, kEpvLin>(a, st) : launch_hist_t<QT, GT, VEC, kMaskRelu, kEpvNone>(a, st);
-  if (lin) return launch_hist_t<QT, GT, VEC, kMaskNone, kEpvLin>(a, st);
-  return bias ? launch_hist_t<QT, GT, VEC, kMaskNone, kEpvBias>(a, st) : launch_hist_t<QT, GT, VEC, kMaskNone, kEpvNone>(a, st);
+    return lin ? launch_hist_t<QT, GT, VEC, kMaskRelu, kEpvLin, NCL>(a, st)
+               : launch_hist_t<QT, GT, VEC, kMaskRelu, kEpvNone, NCL>(a, st);
+  if (lin) return launch_hist_t<QT, GT, VEC, kMaskNone, kEpvLin, NCL>(a, st);
+  return bias ? launch_hist_t<QT, GT, VEC, kMaskNone, kEpvBias, NCL>(a, st)
+              : launch_hist_t<QT, GT, VEC, kMaskNone, kEpvNone, NCL>(a, st);
 }
 
 // True when the histogram kernel serves a backward of this shape (ple_backward.cu).
@@ -804,9 +828,9 @@ template <typename QT, typename GT>
 int launch_backward_dtype(const BwdArgs& a, int vec, cudaStream_t st) {
   if (backward_uses_hist(a.F, a.B, a.D)) {
     switch (a.D) {
-      case 8: return launch_hist_mask<QT, GT, 2>(a, st);
-      case 16: return launch_hist_mask<QT, GT, 4>(a, st);
-      case 24: return launch_hist_mask<QT, GT, 6>(a, st);
+      case 8: return launch_hist_mask<QT, GT, 2, 4>(a, st);
+      case 16: return launch_hist_mask<QT, GT, 4, 4>(a, st);
+      case 24: return launch_hist_mask<QT, GT, 4, 8>(a, st);
       default: break;
     }
   }
