@@ -55,10 +55,9 @@ namespace ple {
 
 constexpr int kHistNC = 4;  // lanes per D row (d_embedding 8 / 16): 8 samples per warp step, 4 steps per batch of 32
 
-// Lane slots per sample row: 4 for d_embedding 8 and 16 (VEC = D / 4 elements each); 8 for d_embedding 24
-// (6 active lanes of 4 elements, 2 idle), whose bin rows are laid out unit-major so that one 128-byte
-// wavefront serves one row and never meets a bank conflict.
-__host__ __device__ constexpr int hist_lanes(int D) { return D == 24 ? 8 : kHistNC; }
+// Lane slots per sample row (the kernel's NCL): 4 for d_embedding 8 and 16 (VEC = D / 4 elements each); 8
+// for d_embedding 24 (6 active lanes of 4 elements, 2 idle), whose bin rows are laid out unit-major so that
+// one 128-byte wavefront serves one row and never meets a bank conflict.
 // Bytes of one bin row of pair units (S / T table, H / U sums).
 __host__ __device__ constexpr int hist_row_bytes(int D) { return D == 24 ? 256 : 8 * D; }
 // 16 warps per CTA (128 registers a thread; measured faster than 12 warps with 168 registers)
@@ -599,7 +598,6 @@ __global__ void __launch_bounds__(kHistThreads, 1)
           if (__any_sync(0xffffffffu, any_tie)) {
 #pragma unroll
             for (int jj = 0; jj < JG; ++jj) {
-          const int j = h * JG + jj;
               const bool tj = (hv[jj] & kRecTie) != 0;
               if (__any_sync(0xffffffffu, tj)) {
                 const int hk = hv[jj] & ~kRecFlags;

@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) ple_bwd_kernel(const BwdArgs a
   constexpr bool LIN = EPIV == kEpvLin;
   constexpr bool ACC = EPIV != kEpvNone;  // per-slot epilogue sums (sum g x or sum g', and sum g)
   constexpr int NP = Row<VEC>::NP;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];  // one declaration per file: the strictest
   const int lgFc = a.lgFc, lgWf = a.lgWf, lgSt = a.lgSt;
   const int Fc = 1 << lgFc, Wf = 1 << lgWf, S_t = 1 << lgSt;
   const int B = a.B, D = a.D;
