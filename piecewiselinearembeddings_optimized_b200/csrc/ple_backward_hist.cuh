@@ -616,17 +616,15 @@ __global__ void __launch_bounds__(kHistThreads, 1)
               }
             }
           }
-#pragma unroll
-          for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 1);
-#pragma unroll
-          for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 2);
-          if constexpr (NC == 8) {
-#pragma unroll
-            for (int jj = 0; jj < JG; ++jj) gx[jj] += __shfl_xor_sync(0xffffffffu, gx[jj], 4);
-          }
-#pragma unroll
-          for (int jj = 0; jj < JG; ++jj)
-            if ((hv[jj] & kRecDead) == 0 && c == 0) sts_f32(gxa + (h * JG + jj) * R * Fc * 4, gx[jj]);
+          static_assert(JG == 2, "the two steps' row sums share one reduction");
+          // even lanes carry step 0's sum, odd lanes step 1's, so every shuffled share is used; the pairs
+          // are summed in the same order as two separate reductions would sum them (bit-identical)
+          const bool odd = (c & 1) != 0;
+          float s1 = (odd ? gx[1] : gx[0]) + __shfl_xor_sync(0xffffffffu, odd ? gx[0] : gx[1], 1);
+          s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+          if constexpr (NC == 8) s1 += __shfl_xor_sync(0xffffffffu, s1, 4);
+          const int hs = odd ? hv[1] : hv[0];
+          if ((hs & kRecDead) == 0 && c < 2) sts_f32(gxa + (h * JG + c) * R * Fc * 4, s1);
         }
         // ---- phase 3: H += q(g'), U += q(t) q(g') into the warp's copy, step by step: the first samples of
         // their bin, then, in a step with a shared bin, the second ones, then, rarely (a bin shared by three
