@@ -11,11 +11,13 @@
 // so that x_ple = q(fma(q(t), S[k], T[k])) (reference forward_cuda.cu:135-176,
 // 258-273).  Then, per tile of samples:
 //   x tile   [S_t][Fc] arrives by cp.async, double-buffered one tile ahead;
-//   phase 1  one thread per (sample, feature): L-probe bin search, {k, q(t), x} -> smem
+//   phase 1  one thread per (sample, feature), two pairs of one feature at a time so
+//            that their searches overlap: L-probe bin search, {k, q(t), x} -> smem
 //            (+ bin-index store for the reference op);
 //   phase 2  one thread per VEC-wide chunk of an output row, each thread on a
 //            fixed column (its epilogue parameters live in registers): one
-//            16-byte record, two table reads, epilogue, streaming store.
+//            16-byte record (read one sample ahead), two table reads, epilogue,
+//            streaming store.
 // The epilogue (none / A / B) and ReLU are template parameters; the inner
 // loop is kept to a minimum of instructions (the kernel is issue-bound
 // before it is bandwidth-bound).  With
@@ -75,31 +77,47 @@ __host__ __device__ __forceinline__ size_t fwd_layout(const FwdArgs& a, FwdLayou
   return off;
 }
 
+// Bin index k of one (sample, feature) pair into the reference op's bin-index output.
+__device__ __forceinline__ void store_bin(const FwdArgs& a, int64_t pair, int k) {
+  if (a.bin_idx_bytes == 1) reinterpret_cast<uint8_t*>(a.bin_idx)[pair] = (uint8_t)k;
+  else if (a.bin_idx_bytes == 2) reinterpret_cast<int16_t*>(a.bin_idx)[pair] = (int16_t)k;
+  else reinterpret_cast<int32_t*>(a.bin_idx)[pair] = k;
+}
+
 // Phase 1 of a tile: per (sample, feature) the bin (L-probe search over the
 // feature's interior edges), the position and the record {k * kstride, q(t), x}.
 template <int L, typename QT>
 __device__ __forceinline__ void fwd_phase1(const FwdArgs& a, const FwdLayout& Ly, const float* sX, int ns, int fc,
                                            int kstride, int64_t t0, int f0, int tid, int nthr) {
   const int lgFc = a.lgFc, Fc = 1 << lgFc, ldK = a.ldK, B = a.B;
-  for (int p = tid; p < (ns << lgFc); p += nthr) {
+  const int np = ns << lgFc;
+  // two pairs a thread at a time (p and p + nthr: the same feature, nthr being a multiple of Fc), so that
+  // their searches overlap
+  for (int p = tid; p < np; p += 2 * nthr) {
     const int i = p & (Fc - 1);
-    const float xv = sX[p];
-    float4 q = make_float4(0.0f, 0.0f, xv, 0.0f);
+    const int p1 = p + nthr;
+    const bool has1 = p1 < np;
+    const float x0 = sX[p];
+    const float x1 = has1 ? sX[p1] : 0.0f;
+    float4 q0 = make_float4(0.0f, 0.0f, x0, 0.0f), q1 = make_float4(0.0f, 0.0f, x1, 0.0f);
     if (i < fc) {
-      const int c = key_count<L>(xv, Ly.sK + i * ldK);
+      const float* keys = Ly.sK + i * ldK;
+      const int c0 = key_count<L>(x0, keys);
+      const int c1 = key_count<L>(x1, keys);
       const int n1 = Ly.sN[i] - 1;
-      const int k = c < n1 ? c : n1;
-      const float2 er = Ly.sL[i * B + k];
-      q.x = __int_as_float(k * kstride);
-      q.y = quantize<QT>((xv - er.x) * er.y);
+      const int k0 = c0 < n1 ? c0 : n1, k1 = c1 < n1 ? c1 : n1;
+      const float2 er0 = Ly.sL[i * B + k0], er1 = Ly.sL[i * B + k1];
+      q0.x = __int_as_float(k0 * kstride);
+      q0.y = quantize<QT>((x0 - er0.x) * er0.y);
+      q1.x = __int_as_float(k1 * kstride);
+      q1.y = quantize<QT>((x1 - er1.x) * er1.y);
       if (a.bin_idx != nullptr) {
-        const int64_t pair = (t0 + (p >> lgFc)) * a.F + f0 + i;
-        if (a.bin_idx_bytes == 1) reinterpret_cast<uint8_t*>(a.bin_idx)[pair] = (uint8_t)k;
-        else if (a.bin_idx_bytes == 2) reinterpret_cast<int16_t*>(a.bin_idx)[pair] = (int16_t)k;
-        else reinterpret_cast<int32_t*>(a.bin_idx)[pair] = k;
+        store_bin(a, (t0 + (p >> lgFc)) * a.F + f0 + i, k0);
+        if (has1) store_bin(a, (t0 + (p1 >> lgFc)) * a.F + f0 + i, k1);
       }
     }
-    Ly.sQ[p] = q;
+    Ly.sQ[p] = q0;
+    if (has1) Ly.sQ[p1] = q1;
   }
 }
 
@@ -235,13 +253,18 @@ ple_fwd_kernel(const FwdArgs a) {
         const int64_t ostep = ostride * s_step;
         const float4* qptr = L.sQ + (s_first << lgFc) + ci;
         const int qstep = s_step << lgFc;
+        // the record of the next sample is read one iteration ahead, so that only the table reads
+        // wait on a shared-memory round trip
+        float4 q = s_first < ns ? *qptr : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 2
-        for (int s = s_first; s < ns; s += s_step, optr += ostep, qptr += qstep) {
-          const float4 q = *qptr;
+        for (int s = s_first; s < ns; s += s_step, optr += ostep) {
           const int off = __float_as_int(q.x);
           const FV<VEC> tv = lds<VEC>(sTc + off);
           const FV<VEC> sv = lds<VEC>(sSc + off);
+          qptr += qstep;
+          const float4 qn = s + s_step < ns ? *qptr : q;
           store_out<OT, VEC>(optr, fwd_chunk<QT, OT, VEC, EPI, RELU>(q.y, tv, sv, q.z, ep0, ep1));
+          q = qn;
         }
       }
     }
