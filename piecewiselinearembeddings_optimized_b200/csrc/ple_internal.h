@@ -37,6 +37,8 @@ struct FwdArgs {
   int epi, relu;
   // filled by the launcher
   int lgFc, n_chunks, S_t, lgk, ldK, x_vec4;
+  // slots of `group` CTAs over the same samples, member j on chunk g * group + j of chunk group g
+  int group, n_groups;
 };
 
 struct BwdArgs {
