@@ -330,8 +330,9 @@ int launch_forward(FwdArgs a, int compute_dtype, int output_dtype, int vec, cuda
   if (vec != 4) vec = 1;
   // feature chunk: power of two, tables within the budget, R = Fc * D / vec <= kFwdMaxThreads.  The larger
   // budget (wider chunks, one CTA per SM) only for fp32 outputs with D <= 16, where it measured faster (c5
-  // shard: 16 features 0.92 ms, 8 features 1.05); elsewhere it measured slower (c4, bf16: 0.30 vs 0.26 ms;
-  // c2, D = 32: 0.126 vs 0.122; c3, D = 64: 0.125 vs 0.117)
+  // shard: 16 features 0.92 ms, 8 features 1.05) before the CTA slots and ties with them (full c5: 6.733 vs
+  // 6.725 ms); elsewhere it measured slower (c4, bf16: 0.30 vs 0.26 ms; c2, D = 32: 0.126 vs 0.122; c3,
+  // D = 64: 0.125 vs 0.117)
   const int nc = a.D / vec;
   int lg = 4;
   const size_t budget = output_dtype == PLE_DTYPE_F32 && a.D <= 16 ? kFwdTableBudgetF32 : kFwdTableBudget;
