@@ -1,8 +1,10 @@
 // ple_forward.cu - fused PLE forward for sm_100a.
 //
-// The grid is persistent (SMs x resident CTAs); CTA j owns an equal contiguous
-// range of the flattened (feature chunk, sample) space - one or a few
-// (chunk of Fc consecutive features, sample range) segments.  Per segment it
+// The grid is persistent (SMs x resident CTAs) and cut into slots of m CTAs;
+// slot j owns an equal contiguous range of the flattened (chunk group, sample)
+// space, and member i of the slot takes chunk g m + i of group g, so that the
+// members read the x pieces of one 128-byte line together.  A CTA has one or a
+// few (chunk of Fc consecutive features, sample range) segments.  Per segment it
 // stages the chunk's search keys (interior edges e_1 .. e_{n-1}, +inf padded
 // to 2^L - 1), {e_k, r_k} pairs and two tables in shared memory, the tables
 // laid out bin-major [k][feature][d]:
