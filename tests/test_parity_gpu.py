@@ -318,10 +318,12 @@ def test_kernels_match_reference_golden(ops, cuda_device, path):
 # ---------------------------------------------------------------- benchmark configurations
 
 @pytest.mark.parametrize("name,n,f", [("c1", None, None), ("c2", None, None), ("c3", None, None),
-                                      ("c4", 4096, None), ("c5", 2048, None)])
+                                      ("c4", 4096, None), ("c5", 2048, None), ("c5", 512, 48), ("c4", 512, 40)])
 def test_configs_match_oracle(ops, cuda_device, name, n, f):
     """c1, c2 and c3 at their full batch (c3: 16,384 rows, ragged and deduplicated bins, D = 64 on the sorted
-    kernel), c4 and c5 on a slice (their full batches are checked by test_full_size_properties)."""
+    kernel), c4 and c5 on a slice (their full batches are checked by test_full_size_properties).  48 features
+    of c5 (3 forward chunks of 16 in slots of 2 CTAs) and 40 of c4 (5 chunks of 8 in slots of 4) leave the
+    last forward slot partly idle."""
     wl = workloads.make_workload(name, n=n, f=f)
     g = workloads.make_grad(wl)
     edges, inv_w, nb = o.pad_bins(wl.bins)
